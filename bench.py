@@ -1,0 +1,452 @@
+#!/usr/bin/env python3
+"""Forward-pass throughput of the Transformer encoder stack on B200s (one JSON line).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2] [--impl ours|reference]
+
+A step is one forward pass of UserOptimizedTransformer over one batch of synthetic inputs with
+the BASELINE configuration's shapes (x ~ N(0,1) and padding lengths from the reference's
+generator, weights from the reference's default init under torch.manual_seed(0)).
+
+Workloads (per GPU; multi-GPU runs are weak-scaled batch shards with no collective in the data
+path, one process per GPU launched by torch.distributed.run):
+  c2 (default)  B=8  S=512    D=768  H=12 F=3072 L=12, padding mask (lengths in [256, 512])
+  c3            B=16 S=2048   D=1024 H=16 F=4096 L=4, causal
+  c5            B=4  S=100000 D=1024 H=16 F=1024 L=2, causal (x8 GPUs = the B=32 configuration)
+  c1            B=2  S=128    D=256  H=4  F=1024 L=2, causal
+  c4            B=1  S=32768  D=2048 H=16 F=8192 L=2, causal (single GPU)
+
+Reported (rank 0): `value` = tokens/s of the whole job with inputs resident in HBM, each of the K
+timed steps bracketed by barrier + synchronize and timed with CUDA events on the launching
+stream, L2 flushed (256 MiB write) before every step, max over ranks; `e2e` = the same forward
+through the public module API with the step's input copied from pinned host memory and the
+output copied back inside the timed region; `roofline` = the dominant kernel (by device time)
+against the measured bf16 tensor peak; `cpu_baseline` = the fp32 CPU restatement of the
+reference (oracle/) on a bounded sample, on the host's cores.
+
+`--impl reference` times the reference computation on the host CPU instead (fp32, all host
+threads, the oracle port of BaselineTransformer.forward) and prints the same line with
+"impl": "reference"; under torch.distributed.run only rank 0 runs it.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+from tiktoktechjam2026track3_b200 import UserOptimizedTransformer  # noqa: E402
+from tiktoktechjam2026track3_b200.cases import BASELINE_CONFIGS, TransformerConfig, generate_random_case  # noqa: E402
+
+METRIC = "forward_tokens_per_sec"
+UNIT = "tokens/s"
+PER_GPU_BATCH = {"c1": 2, "c2": 8, "c3": 16, "c4": 1, "c5": 4}
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse_args(argv=None):
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--workload", default="c2", choices=sorted(BASELINE_CONFIGS))
+    p.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
+    p.add_argument("--cpu-seconds", type=float, default=15.0, help="target CPU time of the CPU baseline sample")
+    return p.parse_args(argv)
+
+
+def workload_config(name: str) -> tuple[TransformerConfig, float]:
+    w = BASELINE_CONFIGS[name]
+    c = w.config
+    cfg = TransformerConfig(PER_GPU_BATCH[name], c.seq_len, c.d_model, c.num_heads, c.ffn_dim, c.num_layers, c.causal)
+    return cfg, w.padding_ratio
+
+
+def measured_peaks() -> tuple[dict, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            data = json.loads(path.read_text())
+            return {"hbm_gbs": float(data["hbm_gbs"]), "bf16_tflops": float(data["bf16_tflops"]),
+                    "bf16_tflops_sustained": float(data.get("bf16_tflops_sustained", data["bf16_tflops"]))}, "measured"
+        except (KeyError, ValueError):
+            pass
+    return dict(FALLBACK_PEAKS, bf16_tflops_sustained=1400.0), "fallback"
+
+
+# ----------------------------------------------------------------------------- algorithmic work
+def gemm_flops(cfg: TransformerConfig) -> dict:
+    t = cfg.batch_size * cfg.seq_len
+    d, f = cfg.d_model, cfg.ffn_dim
+    per_layer = {
+        "gemm_qkv": 2.0 * t * d * 3 * d,
+        "gemm_out": 2.0 * t * d * d,
+        "gemm_ffn_in": 2.0 * t * d * f,
+        "gemm_ffn_out": 2.0 * t * f * d,
+    }
+    return {k: v * cfg.num_layers for k, v in per_layer.items()}
+
+
+def attention_flops(cfg: TransformerConfig, lengths) -> float:
+    lens = [cfg.seq_len] * cfg.batch_size if lengths is None else [int(v) for v in lengths]
+    pairs = sum(n * (n + 1) / 2.0 for n in lens) if cfg.causal else sum(float(n) * n for n in lens)
+    return cfg.num_layers * 4.0 * cfg.d_model * pairs
+
+
+def layernorm_bytes(cfg: TransformerConfig) -> float:
+    t, d, layers = cfg.batch_size * cfg.seq_len, cfg.d_model, cfg.num_layers
+    # first norm reads bf16 x and writes fp32 residual + bf16 (8 B/elt); the other 2L reads fp32, writes bf16 (6 B)
+    return t * d * (8.0 + 6.0 * (2 * layers))
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons of one GPU while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, device: torch.device):
+        props = torch.cuda.get_device_properties(device)
+        self.bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.bus}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "note": "nvidia-smi unavailable"}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, sm_max, power, reasons = [], [], [], set()
+        for line in out.strip().splitlines():
+            parts = [s.strip() for s in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                sm_max.append(float(parts[1]))
+                power.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(self.NAMES, parts[3:7]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": max(sm_max) if sm_max else None,
+            "power_w_max": max(power) if power else None,
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+        }
+
+
+# ----------------------------------------------------------------------------- CPU legs (oracle)
+def cpu_reference_sample(cfg: TransformerConfig, padding_ratio: float, threads: int):
+    """One sequence of the workload through the fp32 CPU restatement of the reference."""
+    from oracle import reference_fp32 as oracle  # CPU baseline / reference arm only
+
+    torch.set_num_threads(threads)
+    sample_cfg = TransformerConfig(1, cfg.seq_len, cfg.d_model, cfg.num_heads, cfg.ffn_dim, cfg.num_layers, cfg.causal)
+    state = oracle.build_reference_state(sample_cfg, 0)
+    x, mask = oracle.generate_random_case(sample_cfg, torch.device("cpu"), torch.float32, 100000, padding_ratio)
+    use_mask = None if padding_ratio <= 0 else mask
+
+    def step():
+        with torch.inference_mode():
+            oracle.forward(state, sample_cfg, x, use_mask, query_chunk=2048)
+
+    return sample_cfg, step
+
+
+def run_cpu_baseline(cfg, padding_ratio, target_seconds: float) -> dict:
+    threads = os.cpu_count() or 1
+    sample_cfg, step = cpu_reference_sample(cfg, padding_ratio, threads)
+    step()  # warm-up
+    times = []
+    t_begin = time.perf_counter()
+    while True:
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_begin > target_seconds or len(times) >= 50:
+            break
+    per = statistics.median(times)
+    tokens = sample_cfg.batch_size * sample_cfg.seq_len
+    return {
+        "value": tokens / per,
+        "unit": UNIT,
+        "cores": threads,
+        "kind": "port",
+        "sample": f"{len(times)} forwards of 1 sequence (S={cfg.seq_len}, L={cfg.num_layers}) in fp32 on CPU "
+                  f"(oracle restatement of BaselineTransformer.forward), median {per * 1e3:.1f} ms",
+    }
+
+
+def run_reference_arm(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cfg, pad = workload_config(args.workload)
+    threads = os.cpu_count() or 1
+    sample_cfg, step = cpu_reference_sample(cfg, pad, threads)
+    for _ in range(max(args.warmup, 0)):
+        step()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    per = sum(times) / len(times)
+    tokens = sample_cfg.batch_size * sample_cfg.seq_len
+    value = tokens / per
+    sample = (f"each step: 1 sequence (S={cfg.seq_len}) of the workload through the fp32 CPU restatement of "
+              f"BaselineTransformer.forward (oracle/reference_fp32.py), {threads} threads")
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": per * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": args.workload, "model": "transformer_encoder", "global_batch": 1,
+                   "seq_len": cfg.seq_len, "d_model": cfg.d_model, "layers": cfg.num_layers,
+                   "parallelism": "cpu", "sample_of_per_gpu_batch": cfg.batch_size},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU arm
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference_arm(args)
+        return
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torch.distributed.run")
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+
+    cfg, pad = workload_config(args.workload)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.manual_seed(0)
+    model = UserOptimizedTransformer(cfg).to(device=device, dtype=torch.bfloat16).eval()
+    x, mask = generate_random_case(cfg, device, torch.bfloat16, 100000 + rank, pad)
+    lengths = mask.sum(1).tolist() if pad > 0 else None
+    use_mask = mask if pad > 0 else mask  # the harness always passes a mask; all-true masks are elided
+    flush = torch.empty(L2_FLUSH_BYTES // 4, device=device, dtype=torch.float32)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            model(x, use_mask)
+        torch.cuda.synchronize()
+
+        # ---------------- device-timed steps (inputs resident in HBM)
+        stream = torch.cuda.current_stream(device)
+        sampler = ClockSampler(device)
+        sampler.start()
+        step_ms = []
+        for _ in range(args.steps):
+            flush.fill_(1.0)
+            barrier()
+            torch.cuda.synchronize()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(stream)
+            model(x, use_mask)
+            end.record(stream)
+            torch.cuda.synchronize()
+            barrier()
+            step_ms.append(start.elapsed_time(end))
+        clocks = sampler.stop()
+        total_ms = torch.tensor([sum(step_ms)], device=device, dtype=torch.float64)
+        if dist is not None:
+            dist.all_reduce(total_ms, op=dist.ReduceOp.MAX)
+        total_ms = float(total_ms.item())
+        ms_per_step = total_ms / args.steps
+        tokens_per_step = cfg.batch_size * cfg.seq_len * world
+        value = tokens_per_step / (ms_per_step / 1e3)
+
+        # ---------------- end to end through the public API, host buffers
+        x_host = x.cpu().pin_memory()
+        m_host = use_mask.cpu().pin_memory()
+        y_host = torch.empty(x.shape, dtype=torch.bfloat16).pin_memory()
+        e2e_ms = []
+        for i in range(args.warmup + args.steps):
+            flush.fill_(1.0)
+            barrier()
+            torch.cuda.synchronize()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(stream)
+            xd = x_host.to(device, non_blocking=True)
+            md = m_host.to(device, non_blocking=True)
+            y = model(xd, md)
+            y_host.copy_(y, non_blocking=True)
+            end.record(stream)
+            torch.cuda.synchronize()
+            barrier()
+            if i >= args.warmup:
+                e2e_ms.append(start.elapsed_time(end))
+        e2e_total = torch.tensor([sum(e2e_ms)], device=device, dtype=torch.float64)
+        if dist is not None:
+            dist.all_reduce(e2e_total, op=dist.ReduceOp.MAX)
+        e2e_per_step = float(e2e_total.item()) / args.steps
+        h2d = x_host.numel() * x_host.element_size() + m_host.numel() * m_host.element_size()
+        d2h = y_host.numel() * y_host.element_size()
+
+        # ---------------- per-kernel device times (roofline of the dominant kernel)
+        model.record_launches(True)
+        reps = 3
+        for _ in range(reps):
+            flush.fill_(1.0)
+            model(x, use_mask)
+        torch.cuda.synchronize()
+        log = model.take_launch_log()
+        model.record_launches(False)
+
+    kind_ms: dict = {}
+    kind_n: dict = {}
+    for kind, s, e in log:
+        kind_ms[kind] = kind_ms.get(kind, 0.0) + s.elapsed_time(e) / reps
+        kind_n[kind] = kind_n.get(kind, 0) + 1
+    flops = gemm_flops(cfg)
+    attn = attention_flops(cfg, lengths)
+    gemm_ms = sum(v for k, v in kind_ms.items() if k.startswith("gemm"))
+    gemm_total = sum(flops.values())
+    peaks, peak_src = measured_peaks()
+    classes = {
+        "gemm_tc_kernel": {"ms": gemm_ms, "work": gemm_total, "bound": "tensor",
+                           "launches": sum(v for k, v in kind_n.items() if k.startswith("gemm")) // reps},
+        "attention_tc_kernel": {"ms": kind_ms.get("attention", 0.0), "work": attn, "bound": "tensor",
+                                "launches": kind_n.get("attention", 0) // reps},
+        "layernorm_vec_kernel": {"ms": kind_ms.get("layernorm", 0.0), "work": layernorm_bytes(cfg), "bound": "hbm",
+                                 "launches": kind_n.get("layernorm", 0) // reps},
+    }
+    kernels = {}
+    for name, c in classes.items():
+        if c["ms"] <= 0:
+            continue
+        if c["bound"] == "tensor":
+            achieved = c["work"] / (c["ms"] / 1e3) / 1e12
+            peak = peaks["bf16_tflops"]
+            unit = "TFLOP/s"
+        else:
+            achieved = c["work"] / (c["ms"] / 1e3) / 1e9
+            peak = peaks["hbm_gbs"]
+            unit = "GB/s"
+        kernels[name] = {"ms_per_step": c["ms"], "launches_per_step": c["launches"], "achieved": achieved,
+                         "unit": unit, "frac": achieved / peak}
+    dominant = max(classes, key=lambda k: classes[k]["ms"])
+    dk = kernels[dominant]
+    roofline = {
+        "kernel": dominant,
+        "bound": classes[dominant]["bound"],
+        "achieved": dk["achieved"],
+        "peak": peaks["bf16_tflops"] if classes[dominant]["bound"] == "tensor" else peaks["hbm_gbs"],
+        "peak_source": f"{peak_src} ({'bf16 burst' if classes[dominant]['bound'] == 'tensor' else 'HBM copy'})",
+        "unit": dk["unit"],
+        "frac": dk["frac"],
+        "traffic": None,
+        "work_per_launch": classes[dominant]["work"] / max(1, classes[dominant]["launches"]),
+    }
+    total_flops = gemm_total + attn
+    mfu = total_flops / (ms_per_step / 1e3) / 1e12 / peaks["bf16_tflops"] * world
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = run_cpu_baseline(cfg, pad, args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_per_step,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": {
+                "workload": args.workload,
+                "model": "transformer_encoder",
+                "global_batch": cfg.batch_size * world,
+                "seq_len": cfg.seq_len,
+                "d_model": cfg.d_model,
+                "heads": cfg.num_heads,
+                "ffn_dim": cfg.ffn_dim,
+                "layers": cfg.num_layers,
+                "causal": cfg.causal,
+                "padding_ratio": pad,
+                "parallelism": f"dp{world} (batch shards, no collective)",
+                "l2": "flushed (256 MiB write) before every timed step",
+            },
+            "roofline": roofline,
+            "kernels": kernels,
+            "model_flops_per_step": total_flops * world,
+            "mfu_of_bf16_peak": mfu,
+            "cpu_baseline": cpu,
+            "e2e": {"value": tokens_per_step / (e2e_per_step / 1e3), "unit": UNIT, "ms_per_step": e2e_per_step,
+                    "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world},
+            "gpu_launches": args.steps * UserOptimizedTransformer.launches_per_forward(cfg.num_layers),
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,100 @@
+/*
+ * b200tx.h — C-ABI of libb200tx.so, the sm_100a (B200) kernels behind the forward pass of the
+ * TikTok TechJam 2026 Track 3 Transformer encoder stack (Sober7135/TikTokTechJam2026Track3).
+ *
+ * The reference computes this forward pass with ATen calls inside
+ * BaselineTransformer.forward (transformer_benchmark/models.py:909-919) and reaches native code
+ * through two FFI styles: ctypes over a C library (transformer_benchmark/cublaslt_linear.py:63-145)
+ * and torch extensions taking tensors (e.g. case6_exact_layer_norm.py:98-121). This header is the
+ * ctypes-style boundary for the whole path: plain pointers, int64 sizes, int status, the CUDA
+ * stream last as void*. No torch types appear here.
+ *
+ * Conventions for every entry point:
+ *   - returns B2_OK (0) on success; B2_E_INVALID (1) for a bad argument, B2_E_UNSUPPORTED (2) for
+ *     a shape/alignment/device the kernels do not cover, B2_E_CUDA (3) for a CUDA error at launch;
+ *     b2_last_error() then describes the failure (per calling thread);
+ *   - pointers are device pointers owned by the caller; the library allocates no device memory,
+ *     keeps no pointer after the call returns (work is enqueued on `stream`) and never
+ *     synchronises the stream;
+ *   - bf16 means IEEE bfloat16 stored as uint16; row-major throughout;
+ *   - device-side pipeline timeouts (a stuck mbarrier wait) do not trap: they set a status word
+ *     read with b2_device_status().
+ */
+#ifndef B200TX_H_
+#define B200TX_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B2_OK 0
+#define B2_E_INVALID 1
+#define B2_E_UNSUPPORTED 2
+#define B2_E_CUDA 3
+
+/* Epilogues of b2_linear_fwd (acc = A W^T in fp32). */
+#define B2_EPI_BIAS 0           /* out bf16 = bf16(acc + bias)                          */
+#define B2_EPI_BIAS_GELU 1      /* out bf16 = bf16(gelu_erf(bf16(acc + bias)))           */
+#define B2_EPI_RESIDUAL 2       /* out f32 (in place) = mask ? out + acc + bias : out    */
+#define B2_EPI_RESIDUAL_ZERO 3  /* out f32 (in place) = mask ? out + acc + bias : 0      */
+#define B2_EPI_STORE_F32 4      /* out f32 = acc (+ bias if non-null)                     */
+
+/* ABI revision of this header (1). */
+int b2_abi_version(void);
+
+/* Message describing the last failed call on this thread ("" if none). */
+const char* b2_last_error(void);
+
+/* Reads (and with clear != 0 resets) the current device's pipeline status word:
+ * 0 = no kernel gave up waiting since the last clear; otherwise (kernel << 16) | (site << 8) |
+ * reason, kernel 2 = linear, 3 = attention. Synchronous: it waits for the device. */
+int b2_device_status(uint32_t* out_status, int clear);
+
+/*
+ * LayerNorm over the last dimension: y = (x - mean) / sqrt(var + eps) * gamma + beta, fp32
+ * statistics, bf16 y. Replaces nn.LayerNorm in BaselineTransformerBlock (models.py:721, 723) and
+ * final_norm (models.py:907) with the padded-row zeroing of models.py:917-918 fused in:
+ * rows with row_mask[r] == 0 get y = 0 (row_mask may be NULL).
+ *   x          [rows, d_model] fp32 (x_is_bf16 = 0) or bf16 (x_is_bf16 = 1)
+ *   gamma,beta [d_model] bf16
+ *   y          [rows, d_model] bf16
+ *   resid_out  NULL, or (x_is_bf16 = 1 only) [rows, d_model] fp32 receiving float(x)
+ */
+int b2_layernorm_fwd(const void* x, int x_is_bf16, const void* gamma, const void* beta, float eps, void* y,
+                     float* resid_out, const uint8_t* row_mask, int64_t rows, int64_t d_model, void* stream);
+
+/*
+ * out = epilogue(A W^T + bias) on tcgen05 tensor cores (fp32 accumulate in TMEM, TMA-fed).
+ * Replaces the nn.Linear calls of a block — packed q/k/v_proj (models.py:51-53), out_proj (:76),
+ * ffn_in and ffn_out (:734) — with the pointwise work after them fused (see B2_EPI_*).
+ *   a    [m, k] bf16;  w [n, k] bf16 (nn.Linear weight layout);  bias [n] bf16 or NULL
+ *   out  [m, ldo] bf16 (B2_EPI_BIAS, B2_EPI_BIAS_GELU) or fp32 (others)
+ *   row_mask [m] uint8 or NULL (residual epilogues only)
+ *   tile_n 0 = choose, or 128 / 256
+ * Requires n % 32 == 0, k % 8 == 0, ldo % 8 == 0, 16-byte aligned pointers, an sm_100 device.
+ */
+int b2_linear_fwd(const void* a, const void* w, const void* bias, int64_t m, int64_t n, int64_t k, int epilogue,
+                  void* out, int64_t ldo, const uint8_t* row_mask, int tile_n, void* stream);
+
+/*
+ * Multi-head self-attention core (BaselineSelfAttention.forward, models.py:55-75) as one
+ * flash-style tcgen05 kernel: scores = q k^T * scale, causal (key > query) and/or padding
+ * (key >= kv_len[b]) masked to -inf, fp32 softmax, context = p v written as bf16 to
+ * ctx[(b*seq_len + s) * ld_ctx + h*head_dim + d]. Query rows at or past kv_len[b] in whole
+ * 128-row tiles are not written.
+ *   qkv     [batch*seq_len, ld_qkv] bf16; head h of Q/K/V at columns q_col/k_col/v_col + h*head_dim
+ *   kv_len  [batch] int32 (valid-key prefix length per sequence) or NULL (= seq_len)
+ * Requires head_dim in {64, 128}, q/k/v_col multiples of 64, ld_qkv % 8 == 0, an sm_100 device.
+ */
+int b2_attention_fwd(const void* qkv, int64_t ld_qkv, int64_t q_col, int64_t k_col, int64_t v_col, int64_t batch,
+                     int64_t seq_len, int64_t num_heads, int64_t head_dim, const int32_t* kv_len, int causal,
+                     float scale, void* ctx, int64_t ld_ctx, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200TX_H_ */

@@ -1,0 +1,67 @@
+"""The C-ABI library loads, exports every symbol include/b200tx.h declares, and rejects bad
+arguments before touching a device (no GPU needed: no compute call is made)."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from tiktoktechjam2026track3_b200 import _capi
+from tiktoktechjam2026track3_b200.build import LIB_PATH, build
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "b200tx.h"
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build()
+    return _capi.load_library()
+
+
+def declared_symbols():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(b2_\w+)\s*\(", text)))
+
+
+def test_header_declares_bound_symbols():
+    assert declared_symbols() == sorted(_capi.SIGNATURES)
+
+
+def test_library_exports_every_declared_symbol(lib):
+    raw = ctypes.CDLL(str(LIB_PATH))
+    for name in declared_symbols():
+        assert hasattr(raw, name), name
+
+
+def test_abi_version(lib):
+    assert lib.b2_abi_version() == 1
+
+
+def test_linear_rejects_null_and_bad_shapes(lib):
+    s = lib.b2_linear_fwd(None, None, None, 128, 128, 64, 0, None, 128, None, 0, None)
+    assert s == 1
+    assert b"null" in lib.b2_last_error()
+    p = ctypes.c_void_p(16)
+    assert lib.b2_linear_fwd(p, p, p, 128, 100, 64, 0, p, 128, None, 0, None) == 2
+    assert b"multiple of 32" in lib.b2_last_error()
+    assert lib.b2_linear_fwd(p, p, p, 128, 128, 60, 0, p, 128, None, 0, None) == 2
+    assert lib.b2_linear_fwd(p, p, p, 128, 128, 64, 9, p, 128, None, 0, None) == 1
+    assert lib.b2_linear_fwd(p, p, p, 128, 128, 64, 0, p, 128, None, 64, None) == 1
+    assert lib.b2_linear_fwd(ctypes.c_void_p(8), p, p, 128, 128, 64, 0, p, 128, None, 0, None) == 2
+    assert b"aligned" in lib.b2_last_error()
+
+
+def test_attention_rejects_unsupported_head_dim(lib):
+    p = ctypes.c_void_p(16)
+    assert lib.b2_attention_fwd(p, 96, 0, 32, 64, 1, 8, 1, 32, None, 1, 0.1, p, 32, None) == 2
+    assert b"head_dim" in lib.b2_last_error()
+    assert lib.b2_attention_fwd(p, 192, 0, 32, 128, 1, 8, 1, 64, None, 1, 0.1, p, 64, None) == 2
+    assert lib.b2_attention_fwd(None, 192, 0, 64, 128, 1, 8, 1, 64, None, 1, 0.1, p, 64, None) == 1
+
+
+def test_layernorm_rejects_bad_arguments(lib):
+    p = ctypes.c_void_p(16)
+    assert lib.b2_layernorm_fwd(None, 0, p, p, 1e-5, p, None, None, 4, 8, None) == 1
+    assert lib.b2_layernorm_fwd(p, 0, p, p, 0.0, p, None, None, 4, 8, None) == 1
+    assert lib.b2_layernorm_fwd(p, 0, p, p, 1e-5, p, None, None, 0, 8, None) == 0  # empty is a no-op

@@ -1,0 +1,186 @@
+"""Kernel-level parity on a B200: each sm_100a kernel, called through the C-ABI, against a plain
+PyTorch fp32 computation of the same op on the same inputs."""
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle import reference_fp32 as oracle
+from tiktoktechjam2026track3_b200 import _capi
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _no_tf32_and_clean_status(cuda_device):
+    torch.backends.cuda.matmul.allow_tf32 = False
+    _capi.device_status(clear=True)
+    yield
+    torch.cuda.synchronize()
+    assert _capi.device_status(clear=True) == 0, "a kernel pipeline wait timed out"
+
+
+def _gen(seed):
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    return g
+
+
+# ---------------------------------------------------------------------------------- LayerNorm
+@pytest.mark.parametrize("rows,d", [(1000, 256), (777, 768), (300, 1024), (129, 2048), (50, 96), (64, 4096)])
+def test_layernorm_fp32_input(rows, d):
+    g = _gen(rows + d)
+    x = torch.randn(rows, d, device="cuda", generator=g) * 3 + 0.5
+    w = (torch.randn(d, device="cuda", generator=g) * 0.2 + 1).bfloat16()
+    b = (torch.randn(d, device="cuda", generator=g) * 0.1).bfloat16()
+    y = torch.empty(rows, d, device="cuda", dtype=torch.bfloat16)
+    _capi.layernorm(x, w, b, 1e-5, y)
+    ref = F.layer_norm(x, (d,), w.float(), b.float(), 1e-5)
+    torch.testing.assert_close(y.float(), ref, atol=1e-2, rtol=8e-3)
+
+
+@pytest.mark.parametrize("d", [256, 1024, 96])
+def test_layernorm_bf16_input_writes_residual_and_masks_rows(d):
+    rows = 333
+    g = _gen(d)
+    x = torch.randn(rows, d, device="cuda", generator=g).bfloat16()
+    w = torch.ones(d, device="cuda", dtype=torch.bfloat16)
+    b = torch.zeros(d, device="cuda", dtype=torch.bfloat16)
+    y = torch.empty(rows, d, device="cuda", dtype=torch.bfloat16)
+    resid = torch.empty(rows, d, device="cuda", dtype=torch.float32)
+    mask = (torch.rand(rows, device="cuda", generator=g) > 0.3).to(torch.uint8)
+    _capi.layernorm(x, w, b, 1e-5, y, resid_out=resid, row_mask=mask)
+    assert torch.equal(resid, x.float())
+    ref = F.layer_norm(x.float(), (d,), None, None, 1e-5)
+    keep = mask.bool()
+    torch.testing.assert_close(y.float()[keep], ref[keep], atol=1e-2, rtol=8e-3)
+    assert torch.all(y[~keep] == 0)
+
+
+# ---------------------------------------------------------------------------------- GEMM
+GEMM_SHAPES = [
+    (128, 256, 64),
+    (200, 384, 200),     # ragged M and K, N not a multiple of 256
+    (4096, 2304, 768),   # C2 packed QKV
+    (1000, 3072, 768),   # C2 ffn_in, ragged M
+    (513, 768, 3072),    # C2 ffn_out, ragged M
+    (2048, 1024, 4096),  # C3 ffn_out
+    (64, 32, 8),         # tiny
+]
+
+
+def _gemm_inputs(m, n, k, seed):
+    g = _gen(seed)
+    a = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(n, k, device="cuda", generator=g) / k**0.5).bfloat16()
+    bias = (torch.randn(n, device="cuda", generator=g) * 0.1).bfloat16()
+    ref = a.float() @ w.float().T + bias.float()
+    return a, w, bias, ref
+
+
+@pytest.mark.parametrize("m,n,k", GEMM_SHAPES)
+def test_gemm_bias_bf16(m, n, k):
+    a, w, bias, ref = _gemm_inputs(m, n, k, 1)
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    _capi.linear(a, w, bias, _capi.EPI_BIAS, out)
+    torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=1e-2)
+
+
+@pytest.mark.parametrize("m,n,k", GEMM_SHAPES[:4])
+def test_gemm_bias_gelu(m, n, k):
+    a, w, bias, ref = _gemm_inputs(m, n, k, 2)
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    _capi.linear(a, w, bias, _capi.EPI_BIAS_GELU, out)
+    expect = F.gelu(ref.bfloat16().float(), approximate="none")
+    torch.testing.assert_close(out.float(), expect, atol=2e-2, rtol=1e-2)
+
+
+@pytest.mark.parametrize("m,n,k", GEMM_SHAPES)
+@pytest.mark.parametrize("zero", [False, True])
+def test_gemm_residual(m, n, k, zero):
+    a, w, bias, ref = _gemm_inputs(m, n, k, 3)
+    g = _gen(4)
+    resid0 = torch.randn(m, n, device="cuda", generator=g)
+    mask = (torch.rand(m, device="cuda", generator=g) > 0.25).to(torch.uint8)
+    resid = resid0.clone()
+    _capi.linear(a, w, bias, _capi.EPI_RESIDUAL_ZERO if zero else _capi.EPI_RESIDUAL, resid, row_mask=mask)
+    keep = mask.bool()[:, None]
+    expect = torch.where(keep, resid0 + ref, torch.zeros_like(resid0) if zero else resid0)
+    torch.testing.assert_close(resid, expect, atol=2e-3, rtol=1e-4)
+
+
+@pytest.mark.parametrize("m,n,k", GEMM_SHAPES[:3])
+def test_gemm_store_f32_and_tile_choice_agree(m, n, k):
+    a, w, bias, ref = _gemm_inputs(m, n, k, 5)
+    out128 = torch.empty(m, n, device="cuda")
+    _capi.linear(a, w, None, _capi.EPI_STORE_F32, out128, tile_n=128)
+    torch.testing.assert_close(out128, ref - bias.float(), atol=2e-3, rtol=1e-4)
+    if n % 256 == 0:
+        out256 = torch.empty(m, n, device="cuda")
+        _capi.linear(a, w, None, _capi.EPI_STORE_F32, out256, tile_n=256)
+        assert torch.equal(out128, out256)
+
+
+def test_gemm_is_row_invariant():
+    """Each output row depends only on its own input row: a sub-batch gives bit-identical rows."""
+    a, w, bias, _ = _gemm_inputs(1536, 1024, 1024, 6)
+    full = torch.empty(1536, 1024, device="cuda", dtype=torch.bfloat16)
+    part = torch.empty(256, 1024, device="cuda", dtype=torch.bfloat16)
+    _capi.linear(a, w, bias, _capi.EPI_BIAS, full)
+    _capi.linear(a[640:896].contiguous(), w, bias, _capi.EPI_BIAS, part)
+    assert torch.equal(full[640:896], part)
+
+
+# ---------------------------------------------------------------------------------- attention
+ATTN_CASES = [
+    # batch, seq, heads, hd, causal, lengths (None = no padding)
+    (2, 128, 2, 64, True, None),
+    (2, 300, 3, 64, False, [300, 129]),
+    (1, 1024, 2, 128, True, None),
+    (3, 200, 2, 128, True, [200, 77, 1]),
+    (2, 2048, 4, 64, True, None),
+    (1, 640, 2, 64, False, None),
+    (2, 512, 12, 64, False, [256, 511]),
+]
+
+
+@pytest.mark.parametrize("batch,seq,heads,hd,causal,lengths", ATTN_CASES)
+def test_attention_matches_fp32_reference(batch, seq, heads, hd, causal, lengths):
+    d = heads * hd
+    g = _gen(seq + hd)
+    qkv = torch.randn(batch * seq, 3 * d, device="cuda", generator=g).bfloat16()
+    kv_len = None
+    key_mask = None
+    if lengths is not None:
+        kv_len = torch.tensor(lengths, device="cuda", dtype=torch.int32)
+        key_mask = torch.arange(seq, device="cuda")[None, :] < kv_len[:, None]
+    ctx = torch.zeros(batch * seq, d, device="cuda", dtype=torch.bfloat16)
+    scale = hd**-0.5
+    _capi.attention(qkv, batch, seq, heads, hd, 0, d, 2 * d, kv_len, causal, scale, ctx)
+
+    t = qkv.float().view(batch, seq, 3, heads, hd)
+    q, k, v = (t[:, :, i].transpose(1, 2) for i in range(3))
+    ref = oracle.attention_core(q, k, v, key_mask, causal, scale, query_chunk=512)
+    ref = ref.transpose(1, 2).reshape(batch, seq, d)
+    got = ctx.float().view(batch, seq, d)
+    for b in range(batch):
+        n = seq if lengths is None else lengths[b]
+        torch.testing.assert_close(got[b, :n], ref[b, :n], atol=2e-2, rtol=2e-2)
+    assert torch.isfinite(got).all()
+
+
+def test_attention_reads_heads_at_column_offsets():
+    """Q/K/V blocks at arbitrary 64-aligned column offsets of a wider row (tensor-parallel shards)."""
+    batch, seq, heads, hd = 1, 256, 2, 64
+    d = heads * hd
+    g = _gen(11)
+    wide = torch.randn(batch * seq, 5 * d, device="cuda", generator=g).bfloat16()
+    ctx = torch.zeros(batch * seq, 2 * d, device="cuda", dtype=torch.bfloat16)
+    _capi.attention(wide, batch, seq, heads, hd, 4 * d, d, 2 * d, None, True, hd**-0.5, ctx)
+    t = wide.float()
+    q = t[:, 4 * d:5 * d].view(batch, seq, heads, hd).transpose(1, 2)
+    k = t[:, d:2 * d].view(batch, seq, heads, hd).transpose(1, 2)
+    v = t[:, 2 * d:3 * d].view(batch, seq, heads, hd).transpose(1, 2)
+    ref = oracle.attention_core(q, k, v, None, True, hd**-0.5).transpose(1, 2).reshape(seq, d)
+    torch.testing.assert_close(ctx[:, :d].float(), ref, atol=2e-2, rtol=2e-2)
+    assert torch.all(ctx[:, d:] == 0)

@@ -1,0 +1,149 @@
+"""Whole-model parity on a B200: UserOptimizedTransformer (all kernels through the C-ABI) against
+the fp32 oracle on the same bf16 weights and inputs, gated by max|y - r| <= 2^-7 * max|r| with
+no NaN/Inf, plus size-independent properties at the full BASELINE sizes."""
+
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import reference_fp32 as oracle
+from tiktoktechjam2026track3_b200 import UserOptimizedTransformer, baseline_gate, _capi
+from tiktoktechjam2026track3_b200.cases import BASELINE_CONFIGS, TransformerConfig
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+MANIFEST = json.loads((GOLDEN / "manifest.json").read_text())
+
+
+@pytest.fixture(autouse=True)
+def _setup(cuda_device):
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    _capi.device_status(clear=True)
+    yield
+    torch.cuda.synchronize()
+    assert _capi.device_status(clear=True) == 0
+
+
+def _model(cfg, state):
+    model = UserOptimizedTransformer(cfg)
+    model.load_state_dict(state, strict=True)
+    return model.to(device="cuda", dtype=torch.bfloat16).eval()
+
+
+def _oracle_gpu(state_bf16, cfg, x_bf16, mask, query_chunk=1024):
+    st = {k: v.to("cuda", torch.float32) for k, v in state_bf16.items()}
+    with torch.inference_mode():
+        return oracle.forward(st, cfg, x_bf16.float(), mask, query_chunk=query_chunk)
+
+
+@pytest.mark.parametrize("name", sorted(MANIFEST))
+def test_model_matches_reference_golden(name):
+    m = MANIFEST[name]
+    cfg = TransformerConfig(m["batch_size"], m["seq_len"], m["d_model"], m["num_heads"], m["ffn_dim"],
+                            m["num_layers"], m["causal"])
+    g = np.load(GOLDEN / f"{name}.npz")
+    state = oracle.build_reference_state(cfg, m["seed"])
+    x, mask = oracle.generate_random_case(cfg, torch.device("cpu"), torch.float32, m["seed"], m["padding_ratio"])
+    model = _model(cfg, state)
+    with torch.inference_mode():
+        y = model(x.to("cuda", torch.bfloat16), mask.cuda())
+    ref = torch.from_numpy(g["out_bf16_inputs"]).cuda()
+    gate = baseline_gate(y, ref)
+    assert gate.passed, gate
+    assert torch.all(y[~mask.cuda()] == 0)
+
+
+def _baseline_case(key, batch=None, seq_len=None):
+    w = BASELINE_CONFIGS[key]
+    c = w.config
+    cfg = TransformerConfig(batch or c.batch_size, seq_len or c.seq_len, c.d_model, c.num_heads, c.ffn_dim,
+                            c.num_layers, c.causal)
+    return cfg, w.padding_ratio
+
+
+@pytest.mark.parametrize(
+    "key,batch,seq_len",
+    [("c1", None, None), ("c2", None, None), ("c3", 2, None), ("c4", None, 8192), ("c5", 1, 16384)],
+)
+def test_model_matches_oracle_on_baseline_configs(key, batch, seq_len):
+    cfg, pad = _baseline_case(key, batch, seq_len)
+    state = oracle.round_state_to_bf16(oracle.build_reference_state(cfg, 0))
+    x, mask = oracle.generate_random_case(cfg, torch.device("cuda"), torch.float32, 0, pad)
+    xb = x.bfloat16()
+    model = _model(cfg, state)
+    with torch.inference_mode():
+        y = model(xb, mask)
+    ref = _oracle_gpu(state, cfg, xb, mask)
+    gate = baseline_gate(y, ref)
+    assert gate.passed, gate
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("key,batch", [("c4", None), ("c5", 2)])
+def test_model_full_length_against_oracle(key, batch):
+    """Full BASELINE sequence length (C4: S=32768, C5: S=100000), checked against the oracle run in
+    fp32 on the GPU (TF32 off)."""
+    cfg, pad = _baseline_case(key, batch)
+    state = oracle.round_state_to_bf16(oracle.build_reference_state(cfg, 0))
+    x, mask = oracle.generate_random_case(cfg, torch.device("cuda"), torch.float32, 0, pad)
+    xb = x.bfloat16()
+    model = _model(cfg, state)
+    with torch.inference_mode():
+        y = model(xb, mask)
+    del model
+    ref = _oracle_gpu(state, cfg, xb, mask, query_chunk=512)
+    gate = baseline_gate(y, ref)
+    assert gate.passed, gate
+
+
+def test_batch_sharding_is_bitwise_invariant():
+    """A batch shard computes exactly what the full batch computes for its sequences."""
+    cfg = TransformerConfig(4, 384, 1024, 16, 1024, 2, True)
+    state = oracle.build_reference_state(cfg, 0)
+    model = _model(cfg, state)
+    x = torch.randn(4, 384, 1024, device="cuda").bfloat16()
+    with torch.inference_mode():
+        full = model(x)
+        part = model(x[1:3].contiguous())
+    assert torch.equal(full[1:3], part)
+
+
+def test_causal_prefix_property_at_long_length():
+    """Causal rows depend only on earlier rows: the first rows of an S=100000 sequence equal the
+    output of its 4096-token prefix, bit for bit."""
+    cfg = TransformerConfig(1, 100000, 1024, 16, 1024, 2, True)
+    state = oracle.build_reference_state(cfg, 0)
+    model = _model(cfg, state)
+    x = torch.randn(1, 100000, 1024, device="cuda").bfloat16()
+    with torch.inference_mode():
+        full = model(x)
+        prefix = model(x[:, :4096].contiguous())
+    assert torch.equal(full[:, :4096], prefix)
+    assert torch.isfinite(full).all()
+
+
+def test_padding_rows_are_zero_and_mask_variants_agree():
+    cfg = TransformerConfig(3, 256, 768, 12, 3072, 2, False)
+    state = oracle.build_reference_state(cfg, 0)
+    model = _model(cfg, state)
+    x, mask = oracle.generate_random_case(cfg, torch.device("cuda"), torch.bfloat16, 5, 0.5)
+    with torch.inference_mode():
+        y = model(x, mask)
+        y_all_true = model(x, torch.ones_like(mask))
+        y_none = model(x, None)
+    assert torch.all(y[~mask] == 0)
+    assert torch.equal(y_all_true, y_none)
+
+
+def test_non_prefix_mask_raises_on_gpu():
+    cfg = TransformerConfig(1, 128, 256, 4, 256, 1, False)
+    model = _model(cfg, oracle.build_reference_state(cfg, 0))
+    mask = torch.ones(1, 128, dtype=torch.bool, device="cuda")
+    mask[0, 5] = False
+    with pytest.raises(NotImplementedError):
+        model(torch.randn(1, 128, 256, device="cuda").bfloat16(), mask)

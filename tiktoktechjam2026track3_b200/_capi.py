@@ -1,0 +1,199 @@
+"""ctypes binding of libb200tx.so (C-ABI declared in include/b200tx.h).
+
+Follows the reference's binding conventions: the library is loaded lazily, once, under a
+lock (transformer_benchmark/native_softmax_bf16.py:16-17, 129-160), every foreign function has
+explicit argtypes/restype, and a non-zero status becomes a RuntimeError carrying the library's
+own message (transformer_benchmark/cublaslt_linear.py:63-145).
+
+There is no fallback: if the library is missing or the device is not an sm_100 GPU, the call
+raises. The wrappers here take torch tensors only to read their pointers, shapes and the current
+CUDA stream; all arithmetic happens in the CUDA kernels.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+from typing import Optional
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libb200tx.so"
+
+EPI_BIAS = 0
+EPI_BIAS_GELU = 1
+EPI_RESIDUAL = 2
+EPI_RESIDUAL_ZERO = 3
+EPI_STORE_F32 = 4
+
+# Every symbol include/b200tx.h declares, with its ctypes signature.
+_i64 = ctypes.c_int64
+_vp = ctypes.c_void_p
+SIGNATURES = {
+    "b2_abi_version": (ctypes.c_int, []),
+    "b2_last_error": (ctypes.c_char_p, []),
+    "b2_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int]),
+    "b2_layernorm_fwd": (
+        ctypes.c_int,
+        [_vp, ctypes.c_int, _vp, _vp, ctypes.c_float, _vp, _vp, _vp, _i64, _i64, _vp],
+    ),
+    "b2_linear_fwd": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _i64, _i64, _i64, ctypes.c_int, _vp, _i64, _vp, ctypes.c_int, _vp],
+    ),
+    "b2_attention_fwd": (
+        ctypes.c_int,
+        [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, ctypes.c_int, ctypes.c_float, _vp, _i64, _vp],
+    ),
+}
+
+_lock = threading.Lock()
+_lib: Optional[ctypes.CDLL] = None
+
+
+def load_library() -> ctypes.CDLL:
+    """Loads libb200tx.so once and binds every entry point; raises if it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build it with `python -m tiktoktechjam2026track3_b200.build` "
+                "(this package has no CPU or PyTorch fallback)"
+            )
+        lib = ctypes.CDLL(str(LIB_PATH))
+        for name, (restype, argtypes) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = restype
+            fn.argtypes = argtypes
+        version = lib.b2_abi_version()
+        if version != 1:
+            raise RuntimeError(f"libb200tx.so ABI version {version}, expected 1")
+        _lib = lib
+        return lib
+
+
+def _check(status: int, what: str) -> None:
+    if status != 0:
+        message = load_library().b2_last_error().decode(errors="replace")
+        raise RuntimeError(f"{what} failed with status {status}: {message}")
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _require(t: torch.Tensor, dtype: torch.dtype, name: str) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (this package has no CPU path)")
+    if t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def device_status(clear: bool = True) -> int:
+    """Pipeline status word of the current device (0 = no kernel gave up waiting)."""
+    lib = load_library()
+    out = ctypes.c_uint32(0)
+    _check(lib.b2_device_status(ctypes.byref(out), 1 if clear else 0), "b2_device_status")
+    return int(out.value)
+
+
+def layernorm(
+    x: torch.Tensor,
+    gamma: torch.Tensor,
+    beta: torch.Tensor,
+    eps: float,
+    y: torch.Tensor,
+    resid_out: Optional[torch.Tensor] = None,
+    row_mask: Optional[torch.Tensor] = None,
+) -> None:
+    """y = LayerNorm(x) in bf16 (see b2_layernorm_fwd)."""
+    d_model = x.shape[-1]
+    rows = x.numel() // d_model
+    if x.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("x must be float32 or bfloat16")
+    _require(x, x.dtype, "x")
+    _require(gamma, torch.bfloat16, "gamma")
+    _require(beta, torch.bfloat16, "beta")
+    _require(y, torch.bfloat16, "y")
+    if y.numel() != x.numel():
+        raise ValueError("y must have x's shape")
+    if resid_out is not None:
+        _require(resid_out, torch.float32, "resid_out")
+    if row_mask is not None:
+        _require(row_mask, torch.uint8, "row_mask")
+    status = load_library().b2_layernorm_fwd(
+        _ptr(x), 1 if x.dtype == torch.bfloat16 else 0, _ptr(gamma), _ptr(beta), float(eps), _ptr(y),
+        _ptr(resid_out), _ptr(row_mask), rows, d_model, _stream_ptr(x.device),
+    )
+    _check(status, "b2_layernorm_fwd")
+
+
+def linear(
+    a: torch.Tensor,
+    w: torch.Tensor,
+    bias: Optional[torch.Tensor],
+    epilogue: int,
+    out: torch.Tensor,
+    row_mask: Optional[torch.Tensor] = None,
+    tile_n: int = 0,
+) -> None:
+    """out = epilogue(a @ w.T + bias) (see b2_linear_fwd)."""
+    _require(a, torch.bfloat16, "a")
+    _require(w, torch.bfloat16, "w")
+    m, k = a.shape[0] if a.dim() == 2 else a.numel() // a.shape[-1], a.shape[-1]
+    n = w.shape[0]
+    if w.shape[1] != k:
+        raise ValueError(f"w has shape {tuple(w.shape)}, expected [n, {k}]")
+    if bias is not None:
+        _require(bias, torch.bfloat16, "bias")
+    out_dtype = torch.bfloat16 if epilogue in (EPI_BIAS, EPI_BIAS_GELU) else torch.float32
+    _require(out, out_dtype, "out")
+    if out.numel() < m * n:
+        raise ValueError("out is too small")
+    ldo = out.shape[-1]
+    if row_mask is not None:
+        _require(row_mask, torch.uint8, "row_mask")
+    status = load_library().b2_linear_fwd(
+        _ptr(a), _ptr(w), _ptr(bias), m, n, k, int(epilogue), _ptr(out), ldo, _ptr(row_mask), int(tile_n),
+        _stream_ptr(a.device),
+    )
+    _check(status, "b2_linear_fwd")
+
+
+def attention(
+    qkv: torch.Tensor,
+    batch: int,
+    seq_len: int,
+    num_heads: int,
+    head_dim: int,
+    q_col: int,
+    k_col: int,
+    v_col: int,
+    kv_len: Optional[torch.Tensor],
+    causal: bool,
+    scale: float,
+    ctx: torch.Tensor,
+) -> None:
+    """ctx = softmax(mask(q k^T * scale)) v per head (see b2_attention_fwd)."""
+    _require(qkv, torch.bfloat16, "qkv")
+    _require(ctx, torch.bfloat16, "ctx")
+    if kv_len is not None:
+        _require(kv_len, torch.int32, "kv_len")
+        if kv_len.numel() != batch:
+            raise ValueError("kv_len must have one entry per sequence")
+    status = load_library().b2_attention_fwd(
+        _ptr(qkv), qkv.shape[-1], q_col, k_col, v_col, batch, seq_len, num_heads, head_dim, _ptr(kv_len),
+        1 if causal else 0, float(scale), _ptr(ctx), ctx.shape[-1], _stream_ptr(qkv.device),
+    )
+    _check(status, "b2_attention_fwd")

@@ -1,0 +1,175 @@
+// C-ABI entry points of libb200tx.so (declared in include/b200tx.h).
+//
+// Conventions (the same ones the reference's ctypes cuBLASLt binding and its torch-extension
+// kernels follow: transformer_benchmark/cublaslt_linear.py:63-145 maps an integer status to an
+// exception; case6_exact_attention.cu:324-379 checks preconditions, launches on the caller's
+// stream and checks the launch):
+//   * every entry point returns int (B2_OK = 0) and takes the cudaStream_t last, as void*;
+//   * pointers are device pointers the caller owns; the library allocates no device memory and
+//     never synchronises the stream;
+//   * on failure, b2_last_error() returns a message for the calling thread.
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "b2_common.cuh"
+#include "layernorm.cuh"
+#include "gemm.cuh"
+#include "attention.cuh"
+
+#define B2_API extern "C" __attribute__((visibility("default")))
+
+namespace b2 {
+
+
+static thread_local char g_last_error[512] = "";
+
+static int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+static int check_launch(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return 0;
+  return fail(3, "%s: CUDA error %d (%s)", what, static_cast<int>(e), cudaGetErrorString(e));
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+cudaError_t make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                              uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return cudaErrorNotSupported;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+int device_sm_count(int device) {
+  static int cache[64] = {0};
+  int& c = cache[device & 63];
+  if (c == 0) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device);
+    c = v > 0 ? v : 148;
+  }
+  return c;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+static bool is_sm100(int* major_out) {
+  int dev = 0, major = 0, minor = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  if (major_out) *major_out = major * 10 + minor;
+  return major == 10 && minor == 0;
+}
+
+}  // namespace b2
+
+using namespace b2;
+
+B2_API int b2_abi_version(void) { return 1; }
+
+B2_API const char* b2_last_error(void) { return g_last_error; }
+
+B2_API int b2_device_status(uint32_t* out_status, int clear) {
+  if (out_status == nullptr) return fail(1, "b2_device_status: out_status is null");
+  uint32_t v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_device_status, sizeof(v));
+  if (e != cudaSuccess) return check_launch(e, "b2_device_status");
+  if (clear && v != 0) {
+    const uint32_t zero = 0;
+    e = cudaMemcpyToSymbol(g_device_status, &zero, sizeof(zero));
+    if (e != cudaSuccess) return check_launch(e, "b2_device_status(clear)");
+  }
+  *out_status = v;
+  return 0;
+}
+
+B2_API int b2_layernorm_fwd(const void* x, int x_is_bf16, const void* gamma, const void* beta, float eps, void* y,
+                            float* resid_out, const uint8_t* row_mask, int64_t rows, int64_t d_model, void* stream) {
+  if (x == nullptr || gamma == nullptr || beta == nullptr || y == nullptr)
+    return fail(1, "b2_layernorm_fwd: null pointer argument");
+  if (rows < 0 || d_model <= 0) return fail(1, "b2_layernorm_fwd: invalid shape rows=%lld d_model=%lld", (long long)rows,
+                                            (long long)d_model);
+  if (!(eps > 0.f)) return fail(1, "b2_layernorm_fwd: eps must be positive");
+  if (rows == 0) return 0;
+  if (rows > (int64_t)0x7fffffff * 8) return fail(2, "b2_layernorm_fwd: too many rows");
+  return check_launch(launch_layernorm(x, x_is_bf16, static_cast<const __nv_bfloat16*>(gamma),
+                                       static_cast<const __nv_bfloat16*>(beta), eps, static_cast<__nv_bfloat16*>(y),
+                                       x_is_bf16 ? resid_out : nullptr, row_mask, rows, d_model,
+                                       static_cast<cudaStream_t>(stream)),
+                      "b2_layernorm_fwd");
+}
+
+B2_API int b2_linear_fwd(const void* a, const void* w, const void* bias, int64_t m, int64_t n, int64_t k, int epilogue,
+                         void* out, int64_t ldo, const uint8_t* row_mask, int tile_n, void* stream) {
+  if (a == nullptr || w == nullptr || out == nullptr) return fail(1, "b2_linear_fwd: null pointer argument");
+  if (m < 0 || n <= 0 || k <= 0) return fail(1, "b2_linear_fwd: invalid shape m=%lld n=%lld k=%lld", (long long)m,
+                                             (long long)n, (long long)k);
+  if (epilogue < 0 || epilogue > 4) return fail(1, "b2_linear_fwd: unknown epilogue %d", epilogue);
+  if (n % 32 != 0) return fail(2, "b2_linear_fwd: n=%lld must be a multiple of 32", (long long)n);
+  if (k % 8 != 0) return fail(2, "b2_linear_fwd: k=%lld must be a multiple of 8", (long long)k);
+  if (ldo < n || ldo % 8 != 0) return fail(2, "b2_linear_fwd: ldo=%lld must be >= n and a multiple of 8", (long long)ldo);
+  if (tile_n != 0 && tile_n != 128 && tile_n != 256) return fail(1, "b2_linear_fwd: tile_n must be 0, 128 or 256");
+  if (tile_n == 256 && n % 256 != 0) return fail(2, "b2_linear_fwd: tile_n=256 needs n %% 256 == 0");
+  if (!aligned16(a) || !aligned16(w) || !aligned16(out) || (bias && !aligned16(bias)))
+    return fail(2, "b2_linear_fwd: pointers must be 16-byte aligned");
+  if (m > 0x7fffff00LL || n > 0x7fffff00LL) return fail(2, "b2_linear_fwd: dimension exceeds 2^31");
+  if (m == 0) return 0;
+  if (!is_sm100(nullptr)) return fail(2, "b2_linear_fwd: needs an sm_100 (B200) device");
+  return check_launch(launch_gemm(static_cast<const __nv_bfloat16*>(a), static_cast<const __nv_bfloat16*>(w),
+                                  static_cast<const __nv_bfloat16*>(bias), m, n, k, epilogue, out, ldo, row_mask, tile_n,
+                                  static_cast<cudaStream_t>(stream)),
+                      "b2_linear_fwd");
+}
+
+B2_API int b2_attention_fwd(const void* qkv, int64_t ld_qkv, int64_t q_col, int64_t k_col, int64_t v_col,
+                            int64_t batch, int64_t seq_len, int64_t num_heads, int64_t head_dim, const int32_t* kv_len,
+                            int causal, float scale, void* ctx, int64_t ld_ctx, void* stream) {
+  if (qkv == nullptr || ctx == nullptr) return fail(1, "b2_attention_fwd: null pointer argument");
+  if (batch < 0 || seq_len < 0 || num_heads <= 0) return fail(1, "b2_attention_fwd: invalid shape");
+  if (head_dim != 64 && head_dim != 128) return fail(2, "b2_attention_fwd: head_dim=%lld not supported (64, 128)",
+                                                     (long long)head_dim);
+  if (q_col % 64 || k_col % 64 || v_col % 64 || q_col < 0 || k_col < 0 || v_col < 0)
+    return fail(2, "b2_attention_fwd: q/k/v column offsets must be non-negative multiples of 64");
+  const int64_t width = num_heads * head_dim;
+  if (q_col + width > ld_qkv || k_col + width > ld_qkv || v_col + width > ld_qkv)
+    return fail(1, "b2_attention_fwd: q/k/v columns exceed ld_qkv");
+  if (ld_qkv % 8 != 0 || ld_ctx % 8 != 0 || ld_ctx < width) return fail(2, "b2_attention_fwd: bad leading dimensions");
+  if (!aligned16(qkv) || !aligned16(ctx)) return fail(2, "b2_attention_fwd: pointers must be 16-byte aligned");
+  if (batch * seq_len > 0x7fffff00LL || batch * num_heads > 0x7fffffffLL || (seq_len + 127) / 128 > 65535)
+    return fail(2, "b2_attention_fwd: problem too large");
+  if (!(scale > 0.f)) return fail(1, "b2_attention_fwd: scale must be positive");
+  if (batch == 0 || seq_len == 0) return 0;
+  if (!is_sm100(nullptr)) return fail(2, "b2_attention_fwd: needs an sm_100 (B200) device");
+  return check_launch(launch_attention(static_cast<const __nv_bfloat16*>(qkv), ld_qkv, q_col, k_col, v_col, batch,
+                                       seq_len, num_heads, head_dim, kv_len, causal, scale,
+                                       static_cast<__nv_bfloat16*>(ctx), ld_ctx, static_cast<cudaStream_t>(stream)),
+                      "b2_attention_fwd");
+}

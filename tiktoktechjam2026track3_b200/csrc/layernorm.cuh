@@ -1,0 +1,190 @@
+// LayerNorm over the last dimension, fp32 statistics, bf16 output.
+//
+// Semantics follow nn.LayerNorm(D, eps) as BaselineTransformerBlock applies it
+// (transformer_benchmark/models.py:721,723 for norm1/norm2 and :907 for final_norm):
+//   y = (x - mean) / sqrt(var + eps) * gamma + beta,  var biased (divide by D).
+// The padded-row zeroing that BaselineTransformer.forward applies after the final norm
+// (models.py:917-918) is fused here: rows whose row_mask byte is 0 are written as zeros.
+//
+// Input is the fp32 residual stream, or the bf16 model input (first norm of the first block); in
+// the bf16 case the kernel also writes the fp32 copy that seeds the residual stream.
+//
+// One warp per row, values held in registers, 16-byte loads / 8-byte stores, so each element
+// is read once and written once: the kernel is HBM-bound at 6 (fp32 in) or 8 (bf16 in + fp32
+// copy + bf16 out) bytes per element.
+#pragma once
+#include "b2_common.cuh"
+
+namespace b2 {
+
+constexpr int kLnWarpsPerBlock = 8;
+
+template <int NV, bool kInBf16>
+__global__ void __launch_bounds__(kLnWarpsPerBlock * 32)
+    layernorm_vec_kernel(const void* __restrict__ x_, const __nv_bfloat16* __restrict__ gamma,
+                         const __nv_bfloat16* __restrict__ beta, float eps, __nv_bfloat16* __restrict__ y,
+                         float* __restrict__ resid_out, const uint8_t* __restrict__ row_mask, int64_t rows) {
+  constexpr int D = NV * 128;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kLnWarpsPerBlock + (threadIdx.x >> 5);
+  if (row >= rows) return;
+
+  float v[NV][4];
+  if constexpr (kInBf16) {
+    const uint2* xr = reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(x_) + row * D);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      uint2 raw = __ldg(xr + i * 32 + lane);
+      __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162*>(&raw.x);
+      __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&raw.y);
+      v[i][0] = __low2float(a);
+      v[i][1] = __high2float(a);
+      v[i][2] = __low2float(b);
+      v[i][3] = __high2float(b);
+    }
+    if (resid_out != nullptr) {
+      float4* rr = reinterpret_cast<float4*>(resid_out + row * D);
+#pragma unroll
+      for (int i = 0; i < NV; ++i) rr[i * 32 + lane] = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+    }
+  } else {
+    const float4* xr = reinterpret_cast<const float4*>(static_cast<const float*>(x_) + row * D);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      float4 t = __ldg(xr + i * 32 + lane);
+      v[i][0] = t.x;
+      v[i][1] = t.y;
+      v[i][2] = t.z;
+      v[i][3] = t.w;
+    }
+  }
+
+  uint2* yr = reinterpret_cast<uint2*>(y + row * D);
+  if (row_mask != nullptr && row_mask[row] == 0) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) yr[i * 32 + lane] = make_uint2(0u, 0u);
+    return;
+  }
+
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) s += (v[i][0] + v[i][1]) + (v[i][2] + v[i][3]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s * (1.0f / D);
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float d = v[i][j] - mean;
+      q = fmaf(d, d, q);
+    }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  const float rstd = rsqrtf(q * (1.0f / D) + eps);
+
+  const uint2* gr = reinterpret_cast<const uint2*>(gamma);
+  const uint2* br = reinterpret_cast<const uint2*>(beta);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    uint2 graw = __ldg(gr + i * 32 + lane);
+    uint2 braw = __ldg(br + i * 32 + lane);
+    __nv_bfloat162 g0 = *reinterpret_cast<__nv_bfloat162*>(&graw.x);
+    __nv_bfloat162 g1 = *reinterpret_cast<__nv_bfloat162*>(&graw.y);
+    __nv_bfloat162 b0 = *reinterpret_cast<__nv_bfloat162*>(&braw.x);
+    __nv_bfloat162 b1 = *reinterpret_cast<__nv_bfloat162*>(&braw.y);
+    const float o0 = fmaf((v[i][0] - mean) * rstd, __low2float(g0), __low2float(b0));
+    const float o1 = fmaf((v[i][1] - mean) * rstd, __high2float(g0), __high2float(b0));
+    const float o2 = fmaf((v[i][2] - mean) * rstd, __low2float(g1), __low2float(b1));
+    const float o3 = fmaf((v[i][3] - mean) * rstd, __high2float(g1), __high2float(b1));
+    yr[i * 32 + lane] = make_uint2(pack_bf16x2(o0, o1), pack_bf16x2(o2, o3));
+  }
+}
+
+// Any D: one warp per row, three strided passes over the row (sum, squared deviations,
+// normalise). Used only for widths that are not a multiple of 128.
+template <bool kInBf16>
+__global__ void __launch_bounds__(kLnWarpsPerBlock * 32)
+    layernorm_any_kernel(const void* __restrict__ x_, const __nv_bfloat16* __restrict__ gamma,
+                         const __nv_bfloat16* __restrict__ beta, float eps, __nv_bfloat16* __restrict__ y,
+                         float* __restrict__ resid_out, const uint8_t* __restrict__ row_mask, int64_t rows,
+                         int64_t D) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kLnWarpsPerBlock + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  auto load = [&](int64_t c) -> float {
+    if constexpr (kInBf16)
+      return __bfloat162float(static_cast<const __nv_bfloat16*>(x_)[row * D + c]);
+    else
+      return static_cast<const float*>(x_)[row * D + c];
+  };
+  if (kInBf16 && resid_out != nullptr)
+    for (int64_t c = lane; c < D; c += 32) resid_out[row * D + c] = load(c);
+  if (row_mask != nullptr && row_mask[row] == 0) {
+    for (int64_t c = lane; c < D; c += 32) y[row * D + c] = __float2bfloat16_rn(0.f);
+    return;
+  }
+  float s = 0.f;
+  for (int64_t c = lane; c < D; c += 32) s += load(c);
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s / static_cast<float>(D);
+  float q = 0.f;
+  for (int64_t c = lane; c < D; c += 32) {
+    const float d = load(c) - mean;
+    q = fmaf(d, d, q);
+  }
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  const float rstd = rsqrtf(q / static_cast<float>(D) + eps);
+  for (int64_t c = lane; c < D; c += 32) {
+    const float o = fmaf((load(c) - mean) * rstd, __bfloat162float(gamma[c]), __bfloat162float(beta[c]));
+    y[row * D + c] = __float2bfloat16_rn(o);
+  }
+}
+
+template <bool kInBf16>
+static cudaError_t launch_layernorm_t(const void* x, const __nv_bfloat16* gamma, const __nv_bfloat16* beta, float eps,
+                                      __nv_bfloat16* y, float* resid_out, const uint8_t* row_mask, int64_t rows,
+                                      int64_t D, cudaStream_t stream) {
+  const dim3 block(kLnWarpsPerBlock * 32);
+  const dim3 grid(static_cast<unsigned>((rows + kLnWarpsPerBlock - 1) / kLnWarpsPerBlock));
+  const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (reinterpret_cast<uintptr_t>(y) % 8 == 0) &&
+                       (reinterpret_cast<uintptr_t>(gamma) % 8 == 0) && (reinterpret_cast<uintptr_t>(beta) % 8 == 0) &&
+                       (resid_out == nullptr || reinterpret_cast<uintptr_t>(resid_out) % 16 == 0);
+#define B2_LN_CASE(NV)                                                                                   \
+  case NV:                                                                                               \
+    layernorm_vec_kernel<NV, kInBf16><<<grid, block, 0, stream>>>(x, gamma, beta, eps, y, resid_out, row_mask, \
+                                                                  rows);                                 \
+    return cudaGetLastError();
+  if (aligned && D % 128 == 0) {
+    switch (D / 128) {
+      B2_LN_CASE(1)
+      B2_LN_CASE(2)
+      B2_LN_CASE(3)
+      B2_LN_CASE(4)
+      B2_LN_CASE(5)
+      B2_LN_CASE(6)
+      B2_LN_CASE(7)
+      B2_LN_CASE(8)
+      B2_LN_CASE(10)
+      B2_LN_CASE(12)
+      B2_LN_CASE(16)
+      B2_LN_CASE(24)
+      B2_LN_CASE(32)
+      default:
+        break;
+    }
+  }
+#undef B2_LN_CASE
+  layernorm_any_kernel<kInBf16><<<grid, block, 0, stream>>>(x, gamma, beta, eps, y, resid_out, row_mask, rows, D);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_layernorm(const void* x, int x_is_bf16, const __nv_bfloat16* gamma, const __nv_bfloat16* beta,
+                             float eps, __nv_bfloat16* y, float* resid_out, const uint8_t* row_mask, int64_t rows,
+                             int64_t D, cudaStream_t stream) {
+  if (x_is_bf16) return launch_layernorm_t<true>(x, gamma, beta, eps, y, resid_out, row_mask, rows, D, stream);
+  return launch_layernorm_t<false>(x, gamma, beta, eps, y, nullptr, row_mask, rows, D, stream);
+}
+
+}  // namespace b2
