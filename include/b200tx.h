@@ -67,6 +67,19 @@ int b2_layernorm_fwd(const void* x, int x_is_bf16, const void* gamma, const void
                      float* resid_out, const uint8_t* row_mask, int64_t rows, int64_t d_model, void* stream);
 
 /*
+ * Residual update fused with the LayerNorm that follows it, for tensor-parallel blocks whose
+ * out_proj / ffn_out partial sums are all-reduced before the residual add (the reference adds
+ * them in BaselineTransformerBlock.forward, models.py:733-737):
+ *   resid = row_mask[r] ? resid + delta + bias : (flags & 1 ? 0 : resid)    (in place, fp32)
+ *   y     = LayerNorm(resid) in bf16; with flags & 2, rows with row_mask[r] == 0 get y = 0
+ *   delta [rows, d_model] fp32 (the all-reduced partial); bias [d_model] bf16 or NULL;
+ *   row_mask [rows] uint8 or NULL (all rows kept). d_model = 128 * {1, 2, 4, 6, 8, 16, 32}.
+ */
+int b2_add_layernorm_fwd(float* resid, const float* delta, const void* bias, const uint8_t* row_mask, int flags,
+                         const void* gamma, const void* beta, float eps, void* y, int64_t rows, int64_t d_model,
+                         void* stream);
+
+/*
  * out = epilogue(A W^T + bias) on tcgen05 tensor cores (fp32 accumulate in TMEM, TMA-fed).
  * Replaces the nn.Linear calls of a block — packed q/k/v_proj (models.py:51-53), out_proj (:76),
  * ffn_in and ffn_out (:734) — with the pointwise work after them fused (see B2_EPI_*).

@@ -1,0 +1,136 @@
+"""Host logic of the multi-GPU plans, on CPU with gloo ranks (world size 2).
+
+The tensor-parallel test runs the exact step sequence of TensorParallelTransformer.forward with
+fp32 torch ops in place of the kernels, on each rank's weight shards from tp_shard_state, with the
+partial sums all-reduced over gloo, and checks the result against the full fp32 oracle.
+"""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+import torch.nn.functional as F
+
+from oracle import reference_fp32 as oracle
+from tiktoktechjam2026track3_b200.cases import TransformerConfig
+from tiktoktechjam2026track3_b200.sharding import batch_shard, tp_check, tp_shard_state
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("batch,world", [(8, 1), (8, 2), (32, 8), (7, 3), (2, 4), (1, 8)])
+def test_batch_shard_partitions_the_batch(batch, world):
+    spans = [batch_shard(batch, world, r) for r in range(world)]
+    assert spans[0][0] == 0 and spans[-1][1] == batch
+    for (a0, a1), (b0, _) in zip(spans, spans[1:]):
+        assert a1 == b0
+    sizes = [b - a for a, b in spans]
+    assert max(sizes) - min(sizes) <= 1
+
+
+def test_tp_check_rejects_uneven_splits():
+    tp_check(TransformerConfig(1, 128, 2048, 16, 8192, 2, True), 8)
+    with pytest.raises(ValueError):
+        tp_check(TransformerConfig(1, 128, 768, 12, 3072, 2, True), 8)
+
+
+def test_tp_shards_cover_the_weights():
+    cfg = TransformerConfig(1, 16, 256, 4, 512, 1, True)
+    state = oracle.build_reference_state(cfg, 0)
+    shards = [tp_shard_state(state, cfg, 2, r)[0] for r in range(2)]
+    q = state["layers.0.attention.q_proj.weight"]
+    assert torch.equal(torch.cat([s["w_qkv"][:128] for s in shards], 0), q)
+    assert torch.equal(torch.cat([s["w_o"] for s in shards], 1), state["layers.0.attention.out_proj.weight"])
+    assert torch.equal(torch.cat([s["w_1"] for s in shards], 0), state["layers.0.ffn_in.weight"])
+    assert torch.equal(torch.cat([s["w_2"] for s in shards], 1), state["layers.0.ffn_out.weight"])
+
+
+def _tp_rank(rank, world, port, cfg, pad, result_queue):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        state = oracle.build_reference_state(cfg, 0)
+        x, mask = oracle.generate_random_case(cfg, torch.device("cpu"), torch.float32, 3, pad)
+        shards = tp_shard_state(state, cfg, world, rank)
+        h_loc, hd = cfg.num_heads // world, cfg.d_model // cfg.num_heads
+        d_loc = h_loc * hd
+        b, s, d = x.shape
+        m = mask.reshape(-1, 1)
+
+        def ln(t, w, bb):
+            return F.layer_norm(t, (d,), w, bb, 1e-5)
+
+        resid = x.reshape(-1, d).clone()
+        y = ln(resid, shards[0]["ln1_w"], shards[0]["ln1_b"])
+        for i, sh in enumerate(shards):
+            qkv = y @ sh["w_qkv"].T + sh["b_qkv"]
+            q, k, v = (qkv[:, j * d_loc:(j + 1) * d_loc].reshape(b, s, h_loc, hd).transpose(1, 2) for j in range(3))
+            ctx = oracle.attention_core(q, k, v, mask, cfg.causal, hd**-0.5).transpose(1, 2).reshape(-1, d_loc)
+            part = ctx @ sh["w_o"].T
+            dist.all_reduce(part)
+            resid = torch.where(m, resid + part + sh["b_o"], resid)
+            y = ln(resid, sh["ln2_w"], sh["ln2_b"])
+            part = F.gelu(y @ sh["w_1"].T + sh["b_1"]) @ sh["w_2"].T
+            dist.all_reduce(part)
+            resid = torch.where(m, resid + part + sh["b_2"], torch.zeros_like(resid))
+            last = i == len(shards) - 1
+            if last:
+                y = torch.where(m, ln(resid, state["final_norm.weight"], state["final_norm.bias"]), 0.0)
+            else:
+                y = ln(resid, shards[i + 1]["ln1_w"], shards[i + 1]["ln1_b"])
+        ref = oracle.forward(state, cfg, x, mask)
+        result_queue.put((rank, float((y.reshape(b, s, d) - ref).abs().max())))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("pad", [0.0, 0.4])
+def test_tensor_parallel_math_matches_full_model_over_gloo(pad):
+    cfg = TransformerConfig(2, 40, 256, 4, 512, 2, True)
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_tp_rank, args=(r, world, port, cfg, pad, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    errs = dict(q.get(timeout=5) for _ in range(world))
+    assert max(errs.values()) < 1e-4, errs
+
+
+def _failing_rank(rank, world, port):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    from datetime import timedelta
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
+    if rank == 1:
+        raise RuntimeError("rank 1 fails between steps")
+    t = torch.ones(4)
+    dist.all_reduce(t)  # rank 0 must not hang: the process-group timeout ends it with an error
+
+
+def test_a_failing_rank_surfaces_as_errors_not_a_hang():
+    world = 2
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_rank, args=(r, world, port)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=90)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert codes[1] not in (0, None)
+    assert codes[0] not in (0, None)

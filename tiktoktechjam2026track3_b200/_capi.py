@@ -38,6 +38,10 @@ SIGNATURES = {
         ctypes.c_int,
         [_vp, ctypes.c_int, _vp, _vp, ctypes.c_float, _vp, _vp, _vp, _i64, _i64, _vp],
     ),
+    "b2_add_layernorm_fwd": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, ctypes.c_int, _vp, _vp, ctypes.c_float, _vp, _i64, _i64, _vp],
+    ),
     "b2_linear_fwd": (
         ctypes.c_int,
         [_vp, _vp, _vp, _i64, _i64, _i64, ctypes.c_int, _vp, _i64, _vp, ctypes.c_int, _vp],
@@ -137,6 +141,42 @@ def layernorm(
         _ptr(resid_out), _ptr(row_mask), rows, d_model, _stream_ptr(x.device),
     )
     _check(status, "b2_layernorm_fwd")
+
+
+ADD_LN_ZERO_ROWS = 1
+ADD_LN_ZERO_Y = 2
+
+
+def add_layernorm(
+    resid: torch.Tensor,
+    delta: torch.Tensor,
+    bias: Optional[torch.Tensor],
+    gamma: torch.Tensor,
+    beta: torch.Tensor,
+    eps: float,
+    y: torch.Tensor,
+    row_mask: Optional[torch.Tensor] = None,
+    flags: int = 0,
+) -> None:
+    """resid = mask ? resid + delta + bias : (resid | 0); y = LayerNorm(resid) (b2_add_layernorm_fwd)."""
+    d_model = resid.shape[-1]
+    rows = resid.numel() // d_model
+    _require(resid, torch.float32, "resid")
+    _require(delta, torch.float32, "delta")
+    _require(gamma, torch.bfloat16, "gamma")
+    _require(beta, torch.bfloat16, "beta")
+    _require(y, torch.bfloat16, "y")
+    if delta.numel() != resid.numel() or y.numel() != resid.numel():
+        raise ValueError("resid, delta and y must have the same number of elements")
+    if bias is not None:
+        _require(bias, torch.bfloat16, "bias")
+    if row_mask is not None:
+        _require(row_mask, torch.uint8, "row_mask")
+    status = load_library().b2_add_layernorm_fwd(
+        _ptr(resid), _ptr(delta), _ptr(bias), _ptr(row_mask), int(flags), _ptr(gamma), _ptr(beta), float(eps),
+        _ptr(y), rows, d_model, _stream_ptr(resid.device),
+    )
+    _check(status, "b2_add_layernorm_fwd")
 
 
 def linear(

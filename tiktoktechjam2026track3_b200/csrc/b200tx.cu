@@ -173,3 +173,25 @@ B2_API int b2_attention_fwd(const void* qkv, int64_t ld_qkv, int64_t q_col, int6
                                        static_cast<__nv_bfloat16*>(ctx), ld_ctx, static_cast<cudaStream_t>(stream)),
                       "b2_attention_fwd");
 }
+
+B2_API int b2_add_layernorm_fwd(float* resid, const float* delta, const void* bias, const uint8_t* row_mask,
+                                int flags, const void* gamma, const void* beta, float eps, void* y, int64_t rows,
+                                int64_t d_model, void* stream) {
+  if (resid == nullptr || delta == nullptr || gamma == nullptr || beta == nullptr || y == nullptr)
+    return fail(1, "b2_add_layernorm_fwd: null pointer argument");
+  if (rows < 0 || d_model <= 0) return fail(1, "b2_add_layernorm_fwd: invalid shape");
+  if (!(eps > 0.f)) return fail(1, "b2_add_layernorm_fwd: eps must be positive");
+  if (flags & ~3) return fail(1, "b2_add_layernorm_fwd: unknown flags %d", flags);
+  if (!add_layernorm_supported(d_model))
+    return fail(2, "b2_add_layernorm_fwd: d_model=%lld not supported (128 * {1,2,4,6,8,16,32})", (long long)d_model);
+  if (!aligned16(resid) || !aligned16(delta) || !aligned16(y) || (bias && !aligned16(bias)) || !aligned16(gamma) ||
+      !aligned16(beta))
+    return fail(2, "b2_add_layernorm_fwd: pointers must be 16-byte aligned");
+  if (rows == 0) return 0;
+  return check_launch(launch_add_layernorm(resid, delta, static_cast<const __nv_bfloat16*>(bias), row_mask, flags & 1,
+                                           (flags >> 1) & 1, static_cast<const __nv_bfloat16*>(gamma),
+                                           static_cast<const __nv_bfloat16*>(beta), eps,
+                                           static_cast<__nv_bfloat16*>(y), rows, d_model,
+                                           static_cast<cudaStream_t>(stream)),
+                      "b2_add_layernorm_fwd");
+}

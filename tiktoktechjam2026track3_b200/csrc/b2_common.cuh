@@ -110,9 +110,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 }
 
 // Named barrier over `nthreads` threads (a multiple of 32) with id `id` (1..15; 0 is
-// __syncthreads).
+// __syncthreads). The non-.aligned form, so lanes may arrive from divergent paths.
 __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+  asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 // Makes this thread's generic-proxy shared-memory writes visible to the async proxy
@@ -144,14 +144,17 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
 // ---------------------------------------------------------------------------------------------
 // Whole warp. Writes the TMEM base address to *slot.
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+  __syncwarp();
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
                "r"(ncols)
                : "memory");
 }
 __device__ __forceinline__ void tmem_relinquish() {
+  __syncwarp();
   asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  __syncwarp();
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 __device__ __forceinline__ void tc_fence_before_sync() {
@@ -182,8 +185,12 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 // Loads 32 consecutive fp32 columns of this thread's TMEM lane (32x32b shape: lane i of the warp
 // reads lane (taddr.lane + i)) and waits for completion inside the same asm statement, so no use
 // of the result can be scheduled before the wait.
+//
+// tcgen05.ld is .sync.aligned: the whole warp must execute it converged. Lanes leave the bounded
+// mbarrier spin independently, so the warp is re-converged here first.
 __device__ __forceinline__ void tmem_load_32cols(uint32_t taddr, float* v) {
   uint32_t r[32];
+  __syncwarp();
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"

@@ -142,6 +142,146 @@ __global__ void __launch_bounds__(kLnWarpsPerBlock * 32)
   }
 }
 
+// Residual update fused with the LayerNorm that follows it (tensor-parallel blocks, where the
+// GEMM epilogue cannot add the residual because the projection output is a per-rank partial sum
+// that is all-reduced first):
+//   r      = row kept ? r + delta + bias : (kZeroRows ? 0 : r)      (written back, fp32)
+//   y      = LayerNorm(r) in bf16, or 0 for masked rows when kZeroY
+// kZeroRows reproduces the block's final masked_fill (models.py:736-737); kZeroY the one after
+// final_norm (models.py:917-918). Masked rows keep x + 0 after attention (models.py:78-79, :733).
+template <int NV, bool kZeroRows, bool kZeroY>
+__global__ void __launch_bounds__(kLnWarpsPerBlock * 32)
+    add_layernorm_vec_kernel(float* __restrict__ resid, const float* __restrict__ delta,
+                             const __nv_bfloat16* __restrict__ bias, const uint8_t* __restrict__ row_mask,
+                             const __nv_bfloat16* __restrict__ gamma, const __nv_bfloat16* __restrict__ beta,
+                             float eps, __nv_bfloat16* __restrict__ y, int64_t rows) {
+  constexpr int D = NV * 128;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kLnWarpsPerBlock + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const bool keep = row_mask == nullptr || row_mask[row] != 0;
+  float4* rr = reinterpret_cast<float4*>(resid + row * D);
+  const float4* dr = reinterpret_cast<const float4*>(delta + row * D);
+  float v[NV][4];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    float4 r = rr[i * 32 + lane];
+    if (keep) {
+      const float4 dd = __ldg(dr + i * 32 + lane);
+      float b[4] = {0.f, 0.f, 0.f, 0.f};
+      if (bias != nullptr) {
+        uint2 braw = __ldg(reinterpret_cast<const uint2*>(bias) + i * 32 + lane);
+        __nv_bfloat162 b0 = *reinterpret_cast<__nv_bfloat162*>(&braw.x);
+        __nv_bfloat162 b1 = *reinterpret_cast<__nv_bfloat162*>(&braw.y);
+        b[0] = __low2float(b0);
+        b[1] = __high2float(b0);
+        b[2] = __low2float(b1);
+        b[3] = __high2float(b1);
+      }
+      r.x += dd.x + b[0];
+      r.y += dd.y + b[1];
+      r.z += dd.z + b[2];
+      r.w += dd.w + b[3];
+      rr[i * 32 + lane] = r;
+    } else if (kZeroRows) {
+      r = make_float4(0.f, 0.f, 0.f, 0.f);
+      rr[i * 32 + lane] = r;
+    }
+    v[i][0] = r.x;
+    v[i][1] = r.y;
+    v[i][2] = r.z;
+    v[i][3] = r.w;
+  }
+  uint2* yr = reinterpret_cast<uint2*>(y + row * D);
+  if (kZeroY && !keep) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) yr[i * 32 + lane] = make_uint2(0u, 0u);
+    return;
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) s += (v[i][0] + v[i][1]) + (v[i][2] + v[i][3]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s * (1.0f / D);
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float d = v[i][j] - mean;
+      q = fmaf(d, d, q);
+    }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  const float rstd = rsqrtf(q * (1.0f / D) + eps);
+  const uint2* gr = reinterpret_cast<const uint2*>(gamma);
+  const uint2* br = reinterpret_cast<const uint2*>(beta);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    uint2 graw = __ldg(gr + i * 32 + lane);
+    uint2 braw = __ldg(br + i * 32 + lane);
+    __nv_bfloat162 g0 = *reinterpret_cast<__nv_bfloat162*>(&graw.x);
+    __nv_bfloat162 g1 = *reinterpret_cast<__nv_bfloat162*>(&graw.y);
+    __nv_bfloat162 b0 = *reinterpret_cast<__nv_bfloat162*>(&braw.x);
+    __nv_bfloat162 b1 = *reinterpret_cast<__nv_bfloat162*>(&braw.y);
+    const float o0 = fmaf((v[i][0] - mean) * rstd, __low2float(g0), __low2float(b0));
+    const float o1 = fmaf((v[i][1] - mean) * rstd, __high2float(g0), __high2float(b0));
+    const float o2 = fmaf((v[i][2] - mean) * rstd, __low2float(g1), __low2float(b1));
+    const float o3 = fmaf((v[i][3] - mean) * rstd, __high2float(g1), __high2float(b1));
+    yr[i * 32 + lane] = make_uint2(pack_bf16x2(o0, o1), pack_bf16x2(o2, o3));
+  }
+}
+
+template <bool kZeroRows, bool kZeroY>
+static cudaError_t launch_add_layernorm_t(float* resid, const float* delta, const __nv_bfloat16* bias,
+                                          const uint8_t* row_mask, const __nv_bfloat16* gamma,
+                                          const __nv_bfloat16* beta, float eps, __nv_bfloat16* y, int64_t rows,
+                                          int64_t D, cudaStream_t stream) {
+  const dim3 block(kLnWarpsPerBlock * 32);
+  const dim3 grid(static_cast<unsigned>((rows + kLnWarpsPerBlock - 1) / kLnWarpsPerBlock));
+#define B2_ALN_CASE(NV)                                                                                          \
+  case NV:                                                                                                       \
+    add_layernorm_vec_kernel<NV, kZeroRows, kZeroY>                                                              \
+        <<<grid, block, 0, stream>>>(resid, delta, bias, row_mask, gamma, beta, eps, y, rows);                   \
+    return cudaGetLastError();
+  switch (D / 128) {
+    B2_ALN_CASE(1)
+    B2_ALN_CASE(2)
+    B2_ALN_CASE(4)
+    B2_ALN_CASE(6)
+    B2_ALN_CASE(8)
+    B2_ALN_CASE(16)
+    B2_ALN_CASE(32)
+    default:
+      return cudaErrorInvalidValue;
+  }
+#undef B2_ALN_CASE
+}
+
+// Widths the fused residual + LayerNorm kernel is instantiated for (D = 128 * NV).
+inline bool add_layernorm_supported(int64_t D) {
+  if (D % 128 != 0) return false;
+  switch (D / 128) {
+    case 1: case 2: case 4: case 6: case 8: case 16: case 32:
+      return true;
+    default:
+      return false;
+  }
+}
+
+cudaError_t launch_add_layernorm(float* resid, const float* delta, const __nv_bfloat16* bias, const uint8_t* row_mask,
+                                 int zero_rows, int zero_y, const __nv_bfloat16* gamma, const __nv_bfloat16* beta,
+                                 float eps, __nv_bfloat16* y, int64_t rows, int64_t D, cudaStream_t stream) {
+  if (zero_rows && zero_y)
+    return launch_add_layernorm_t<true, true>(resid, delta, bias, row_mask, gamma, beta, eps, y, rows, D, stream);
+  if (zero_rows)
+    return launch_add_layernorm_t<true, false>(resid, delta, bias, row_mask, gamma, beta, eps, y, rows, D, stream);
+  if (zero_y)
+    return launch_add_layernorm_t<false, true>(resid, delta, bias, row_mask, gamma, beta, eps, y, rows, D, stream);
+  return launch_add_layernorm_t<false, false>(resid, delta, bias, row_mask, gamma, beta, eps, y, rows, D, stream);
+}
+
 template <bool kInBf16>
 static cudaError_t launch_layernorm_t(const void* x, const __nv_bfloat16* gamma, const __nv_bfloat16* beta, float eps,
                                       __nv_bfloat16* y, float* resid_out, const uint8_t* row_mask, int64_t rows,

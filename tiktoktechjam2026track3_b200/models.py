@@ -75,6 +75,49 @@ def _param_key(t: torch.Tensor) -> Tuple[int, int, torch.device, torch.dtype]:
     return (t.data_ptr(), t._version, t.device, t.dtype)
 
 
+class MaskLengths:
+    """Turns the harness's valid-token mask into what the kernels take, with a one-entry cache.
+
+    Returns (None, None) for no mask or an all-true mask (the reference's masked_fill calls are
+    then no-ops, and its candidate elides such masks the same way, models.py:1137-1161), and
+    (kv_len int32 [B], row_mask uint8 [B*S]) for a prefix mask (positions < length, the form
+    generate_random_case produces, cases.py:87-97). Any other mask raises NotImplementedError.
+    The result is reused while the same mask storage is passed with an unchanged version counter
+    (inference tensors carry no version counter and are re-derived on every call).
+    """
+
+    def __init__(self) -> None:
+        self._cache: Optional[tuple] = None
+
+    def __call__(
+        self, valid_token_mask: Optional[torch.Tensor], batch: int, seq_len: int
+    ) -> Tuple[Optional[torch.Tensor], Optional[torch.Tensor]]:
+        if valid_token_mask is None:
+            return None, None
+        m = valid_token_mask
+        if m.dtype != torch.bool or tuple(m.shape) != (batch, seq_len):
+            raise ValueError(f"valid_token_mask must be bool [{batch}, {seq_len}], got {m.dtype} {tuple(m.shape)}")
+        versioned = not m.is_inference()
+        key = None
+        if versioned:
+            key = (m.data_ptr(), m._version, tuple(m.shape), tuple(m.stride()), m.device)
+            if self._cache is not None and self._cache[0] == key:
+                return self._cache[1]
+        lengths = m.sum(dim=1, dtype=torch.int32)
+        positions = torch.arange(seq_len, device=m.device, dtype=torch.int32)
+        if not torch.equal(m, positions[None, :] < lengths[:, None]):
+            raise NotImplementedError(
+                "valid_token_mask must mark a prefix of each sequence (the form generate_random_case produces)"
+            )
+        if bool((lengths == seq_len).all()):
+            result: Tuple[Optional[torch.Tensor], Optional[torch.Tensor]] = (None, None)
+        else:
+            result = (lengths.contiguous(), m.reshape(-1).contiguous().view(torch.uint8))
+        if versioned:
+            self._cache = (key, result)
+        return result
+
+
 class UserOptimizedTransformer(nn.Module):
     """Transformer encoder stack forward on B200 tensor cores (drop-in for the reference slot)."""
 
@@ -89,7 +132,7 @@ class UserOptimizedTransformer(nn.Module):
         self.final_norm = nn.LayerNorm(config.d_model)
         self._packed: Optional[List[_PackedBlock]] = None
         self._packed_key: Optional[tuple] = None
-        self._mask_cache: Optional[tuple] = None
+        self._mask_lengths = MaskLengths()
         self._launch_log: Optional[list] = None
 
     # ------------------------------------------------------------------ weights
@@ -126,36 +169,8 @@ class UserOptimizedTransformer(nn.Module):
     def mask_to_lengths(
         self, valid_token_mask: Optional[torch.Tensor], batch: int, seq_len: int
     ) -> Tuple[Optional[torch.Tensor], Optional[torch.Tensor]]:
-        """(kv_len int32 [B] or None, row_mask uint8 [B*S] or None) for a prefix mask.
-
-        Returns (None, None) for no mask or an all-true mask (the reference's masked_fill calls are
-        then no-ops). Raises NotImplementedError for masks that are not prefixes. The result is
-        cached for a mask tensor whose storage and version are unchanged.
-        """
-        if valid_token_mask is None:
-            return None, None
-        m = valid_token_mask
-        if m.dtype != torch.bool or tuple(m.shape) != (batch, seq_len):
-            raise ValueError(f"valid_token_mask must be bool [{batch}, {seq_len}], got {m.dtype} {tuple(m.shape)}")
-        versioned = not m.is_inference()
-        if versioned and self._mask_cache is not None:
-            key, result = self._mask_cache
-            if key == (m.data_ptr(), m._version, tuple(m.shape), tuple(m.stride()), m.device):
-                return result
-        lengths = m.sum(dim=1, dtype=torch.int32)
-        positions = torch.arange(seq_len, device=m.device, dtype=torch.int32)
-        prefix = torch.equal(m, positions[None, :] < lengths[:, None])
-        if not prefix:
-            raise NotImplementedError(
-                "valid_token_mask must mark a prefix of each sequence (the form generate_random_case produces)"
-            )
-        if bool((lengths == seq_len).all()):
-            result: Tuple[Optional[torch.Tensor], Optional[torch.Tensor]] = (None, None)
-        else:
-            result = (lengths.contiguous(), m.reshape(-1).contiguous().view(torch.uint8))
-        if versioned:
-            self._mask_cache = ((m.data_ptr(), m._version, tuple(m.shape), tuple(m.stride()), m.device), result)
-        return result
+        """(kv_len int32 [B] or None, row_mask uint8 [B*S] or None); see MaskLengths."""
+        return self._mask_lengths(valid_token_mask, batch, seq_len)
 
     # ------------------------------------------------------------------ launch timing hook
     def record_launches(self, enabled: bool) -> None:
