@@ -431,6 +431,7 @@ def main() -> None:
                 "padding_ratio": pad,
                 "parallelism": f"dp{world} (batch shards, no collective)",
                 "l2": "flushed (256 MiB write) before every timed step",
+                "launches": "first/final LayerNorm eager, the block launches replayed from a CUDA graph",
             },
             "roofline": roofline,
             "kernels": kernels,

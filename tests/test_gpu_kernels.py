@@ -184,3 +184,28 @@ def test_attention_reads_heads_at_column_offsets():
     ref = oracle.attention_core(q, k, v, None, True, hd**-0.5).transpose(1, 2).reshape(seq, d)
     torch.testing.assert_close(ctx[:, :d].float(), ref, atol=2e-2, rtol=2e-2)
     assert torch.all(ctx[:, d:] == 0)
+
+
+# ---------------------------------------------------------------------------------- fused add + LayerNorm
+@pytest.mark.parametrize("d", [256, 768, 1024, 2048])
+@pytest.mark.parametrize("flags", [0, 1, 3])
+def test_add_layernorm(d, flags):
+    rows = 517
+    g = _gen(d + flags)
+    resid0 = torch.randn(rows, d, device="cuda", generator=g)
+    delta = torch.randn(rows, d, device="cuda", generator=g)
+    bias = (torch.randn(d, device="cuda", generator=g) * 0.1).bfloat16()
+    w = (torch.randn(d, device="cuda", generator=g) * 0.2 + 1).bfloat16()
+    b = (torch.randn(d, device="cuda", generator=g) * 0.1).bfloat16()
+    mask = (torch.rand(rows, device="cuda", generator=g) > 0.3).to(torch.uint8)
+    resid = resid0.clone()
+    y = torch.empty(rows, d, device="cuda", dtype=torch.bfloat16)
+    _capi.add_layernorm(resid, delta, bias, w, b, 1e-5, y, row_mask=mask, flags=flags)
+    keep = mask.bool()[:, None]
+    other = torch.zeros_like(resid0) if flags & 1 else resid0
+    expect_r = torch.where(keep, resid0 + delta + bias.float(), other)
+    torch.testing.assert_close(resid, expect_r, atol=1e-5, rtol=1e-6)
+    expect_y = F.layer_norm(expect_r, (d,), w.float(), b.float(), 1e-5)
+    if flags & 2:
+        expect_y = torch.where(keep, expect_y, torch.zeros_like(expect_y))
+    torch.testing.assert_close(y.float(), expect_y, atol=1e-2, rtol=8e-3)

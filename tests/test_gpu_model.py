@@ -147,3 +147,37 @@ def test_non_prefix_mask_raises_on_gpu():
     mask[0, 5] = False
     with pytest.raises(NotImplementedError):
         model(torch.randn(1, 128, 256, device="cuda").bfloat16(), mask)
+
+
+def test_graph_replay_equals_eager_launches():
+    cfg = TransformerConfig(3, 256, 768, 12, 3072, 2, False)
+    model = _model(cfg, oracle.build_reference_state(cfg, 0))
+    x, mask = oracle.generate_random_case(cfg, torch.device("cuda"), torch.bfloat16, 9, 0.5)
+    with torch.inference_mode():
+        model.use_cuda_graph = True
+        a = model(x, mask)
+        b = model(x * 0.5, mask)  # replay with new inputs
+        x2, mask2 = oracle.generate_random_case(cfg, torch.device("cuda"), torch.bfloat16, 10, 0.5)
+        c = model(x2, mask2)  # new mask values, same shape
+        model.use_cuda_graph = False
+        a_e = model(x, mask)
+        b_e = model(x * 0.5, mask)
+        c_e = model(x2, mask2)
+    assert torch.equal(a, a_e) and torch.equal(b, b_e) and torch.equal(c, c_e)
+    assert not torch.equal(a, b)
+
+
+def test_weight_update_recaptures_graph():
+    cfg = TransformerConfig(1, 128, 256, 4, 512, 1, True)
+    model = _model(cfg, oracle.build_reference_state(cfg, 0))
+    x = torch.randn(1, 128, 256, device="cuda").bfloat16()
+    with torch.inference_mode():
+        a = model(x)
+    with torch.no_grad():
+        model.layers[0].ffn_out.bias.add_(1.0)
+    with torch.inference_mode():
+        b = model(x)
+        model.use_cuda_graph = False
+        b_e = model(x)
+    assert not torch.equal(a, b)
+    assert torch.equal(b, b_e)

@@ -51,18 +51,28 @@ constexpr int kAttnSoftmaxThreads = 256;
 
 template <int HD>
 struct AttnCfg {
+  static constexpr int kBoxBytes = 128 * 128;  // one 128-row x 64-column bf16 box
   static constexpr int kBoxes = HD / 64;
   static constexpr int kTileBytes = 128 * HD * 2;
   static constexpr int kKvStages = 2;
   static constexpr int kPBufs = HD == 128 ? 1 : 2;
   static constexpr int kPBytes = 128 * 128 * 2;
+  // head_dim 64: the P.V MMA also produces the softmax row sums. Each V stage is followed by a
+  // 64-column block of bf16 ones (the MN-major operand's next N block, LBO = one box), the MMA
+  // runs with N = 64 + 16, and columns 64..79 of O_j hold sum_k P_j[r, k] in fp32 (the sum of
+  // exactly the bf16 weights that multiply V). head_dim 128 has no shared-memory room for that
+  // and sums in registers.
+  static constexpr bool kTcRowSum = HD == 64;
+  static constexpr int kVStageBytes = kTileBytes + (kTcRowSum ? kBoxBytes : 0);
+  static constexpr int kON = HD + (kTcRowSum ? 16 : 0);
   static constexpr int kTmemCols = 512;
   static constexpr int kSCol = 0;
   static constexpr int kOCol = 256;
+  static constexpr int kOStride = 128;
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kOffQ + kTileBytes;
   static constexpr int kOffV = kOffK + kKvStages * kTileBytes;
-  static constexpr int kOffP = kOffV + kKvStages * kTileBytes;
+  static constexpr int kOffP = kOffV + kKvStages * kVStageBytes;
   static constexpr int kOffRed = kOffP + kPBufs * kPBytes;             // float [2][2][128] row maxima
   static constexpr int kOffSum = kOffRed + 2 * 2 * 128 * 4;            // float [2][128] row sums
   static constexpr int kOffBar = kOffSum + 2 * 128 * 4;
@@ -77,16 +87,20 @@ __device__ __forceinline__ void softmax_wait(uint64_t* bar, uint32_t parity, uin
   if (alive && !mbar_wait(bar, parity, abort_flag, kKernelAttention, site)) alive = false;
 }
 
-// O_acc = O_acc * a + O_i, where O_i = P_i V_i sits in TMEM output buffer (i & 1); `t_cols` is this
-// thread's TMEM lane with the column of its hd half in output buffer 0.
+// O_acc = O_acc * a + O_i, where O_i = P_i V_i sits in TMEM output buffer (i & 1); `t_lane` is
+// this thread's TMEM lane at column 0, `grp` its hd half. With tensor-core row sums the running
+// sum l_acc gets the same update from the row-sum column of O_i.
 template <int HD>
-__device__ __forceinline__ void accumulate_o(float (&o_acc)[HD / 2], int i, float a, uint64_t* o_full,
-                                             uint64_t* o_empty, uint32_t t_cols, int lane, bool& alive,
-                                             volatile int* abort_flag) {
+__device__ __forceinline__ void accumulate_o(float (&o_acc)[HD / 2], float& l_acc, int i, float a,
+                                             uint64_t* o_full, uint64_t* o_empty, uint32_t t_lane, int grp,
+                                             int lane, bool& alive, volatile int* abort_flag) {
+  using Cfg = AttnCfg<HD>;
   const int ob = i & 1;
   softmax_wait(&o_full[ob], (i >> 1) & 1, 9, alive, abort_flag);
   tc_fence_after_sync();
-  const uint32_t t = t_cols + ob * HD;
+  const uint32_t t_buf = t_lane + Cfg::kOCol + ob * Cfg::kOStride;
+  const uint32_t t = t_buf + grp * (HD / 2);
+  if constexpr (Cfg::kTcRowSum) l_acc = fmaf(l_acc, a, tmem_load_1col(t_buf + HD));
 #pragma unroll
   for (int cc = 0; cc < HD / 64; ++cc) {
     float v[32];
@@ -103,7 +117,7 @@ template <int HD>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnParams p) {
   using Cfg = AttnCfg<HD>;
-  constexpr int kBoxBytes = 128 * 128;  // one 128-row x 64-column bf16 box
+  constexpr int kBoxBytes = Cfg::kBoxBytes;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* s_q = smem + Cfg::kOffQ;
@@ -164,6 +178,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
     tmem_relinquish();
   }
+  if constexpr (Cfg::kTcRowSum) {
+    // bf16 1.0 everywhere in the ones blocks (so the swizzle does not matter), made visible to
+    // the tensor core's async-proxy reads.
+    for (int st = 0; st < Cfg::kKvStages; ++st) {
+      uint4* ones = reinterpret_cast<uint4*>(s_v + st * Cfg::kVStageBytes + Cfg::kTileBytes);
+      for (int i = threadIdx.x; i < kBoxBytes / 16; i += kAttnThreads)
+        ones[i] = make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
+    }
+    fence_proxy_async_smem();
+  }
   tc_fence_before_sync();
   __syncthreads();
   tc_fence_after_sync();
@@ -200,7 +224,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         mbar_arrive_expect_tx(&v_full[st], Cfg::kTileBytes);
 #pragma unroll
         for (int c = 0; c < Cfg::kBoxes; ++c)
-          tma_load_2d(s_v + st * Cfg::kTileBytes + c * kBoxBytes, &tm_qkv, &v_full[st], vc + c * 64, krow);
+          tma_load_2d(s_v + st * Cfg::kVStageBytes + c * kBoxBytes, &tm_qkv, &v_full[st], vc + c * 64, krow);
         ++issued_v;
       }
       if (!ok) {
@@ -219,7 +243,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // ---------------- UMMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc_bf16_f32(128, 128, 0, 0);
-      constexpr uint32_t idesc_o = make_idesc_bf16_f32(128, HD, 0, 1);
+      constexpr uint32_t idesc_o = make_idesc_bf16_f32(128, Cfg::kON, 0, 1);
       bool ok = mbar_wait(q_full, 0, abort_flag, kKernelAttention, 3);
       if (ok) tc_fence_after_sync();
       const uint32_t q_addr = smem_u32(s_q);
@@ -251,9 +275,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           if (!mbar_wait(&p_full[pb], pph, abort_flag, kKernelAttention, 7)) break;
           if (!mbar_wait(&o_empty[st], ph ^ 1u, abort_flag, kKernelAttention, 8)) break;
           tc_fence_after_sync();
-          const uint32_t d = tmem_base + Cfg::kOCol + st * HD;
+          const uint32_t d = tmem_base + Cfg::kOCol + st * Cfg::kOStride;
           const uint32_t p_addr = smem_u32(s_p + pb * Cfg::kPBytes);
-          const uint32_t v_addr = smem_u32(s_v + st * Cfg::kTileBytes);
+          const uint32_t v_addr = smem_u32(s_v + st * Cfg::kVStageBytes);
 #pragma unroll
           for (int kk = 0; kk < 128 / 16; ++kk) {
             const uint64_t a_desc = make_sdesc_sw128(p_addr + (kk >> 2) * kBoxBytes + (kk & 3) * 32, 16, 1024);
@@ -285,7 +309,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
     for (int k = 0; k < kOHalf; ++k) o_acc[k] = 0.f;
     float m_run = -INFINITY;  // running row maximum of raw scores
-    float l_run = 0.f;        // this thread's share of the running row sum
+    float l_run = 0.f;        // register row sum (head_dim 128): this thread's 64 columns
+    float l_acc = 0.f;        // tensor-core row sum (head_dim 64): whole row
     float alpha_prev = 0.f;
     bool alive = true;  // false after any wait gave up; the loop still runs to keep barriers matched
 
@@ -309,9 +334,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
         for (int k = 0; k < 64; ++k) s[k] = (k < n_valid) ? s[k] : -INFINITY;
       }
-      float pmax = s[0];
+      float pmax = max3f(s[0], s[1], s[2]);
 #pragma unroll
-      for (int k = 1; k < 64; ++k) pmax = fmaxf(pmax, s[k]);
+      for (int k = 3; k < 63; k += 2) pmax = max3f(pmax, s[k], s[k + 1]);
+      pmax = fmaxf(pmax, s[63]);
       float* red = red_max + (j & 1) * 256;
       red[grp * 128 + r] = pmax;
       named_barrier_sync(1, kAttnSoftmaxThreads);
@@ -335,7 +361,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int k = 0; k < 4; ++k) {
           const float e0 = fast_exp2(fmaf(s[8 * ch + 2 * k], c, neg_mc));
           const float e1 = fast_exp2(fmaf(s[8 * ch + 2 * k + 1], c, neg_mc));
-          lsum += e0 + e1;
+          if constexpr (!Cfg::kTcRowSum) lsum += e0 + e1;
           w[k] = pack_bf16x2(e0, e1);
         }
         *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
@@ -347,17 +373,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (lane == 0) mbar_arrive(&p_full[pb]);
 
       if (j >= 1)
-        accumulate_o<HD>(o_acc, j - 1, alpha_prev, o_full, o_empty, t_lane + Cfg::kOCol + grp * kOHalf, lane, alive,
-                         abort_flag);
+        accumulate_o<HD>(o_acc, l_acc, j - 1, alpha_prev, o_full, o_empty, t_lane, grp, lane, alive, abort_flag);
       alpha_prev = alpha;
     }
     if (n_kv >= 1)
-      accumulate_o<HD>(o_acc, n_kv - 1, alpha_prev, o_full, o_empty, t_lane + Cfg::kOCol + grp * kOHalf, lane, alive,
-                       abort_flag);
+      accumulate_o<HD>(o_acc, l_acc, n_kv - 1, alpha_prev, o_full, o_empty, t_lane, grp, lane, alive, abort_flag);
 
-    red_sum[grp * 128 + r] = l_run;
-    named_barrier_sync(1, kAttnSoftmaxThreads);
-    const float l_tot = l_run + red_sum[(grp ^ 1) * 128 + r];
+    float l_tot = l_acc;
+    if constexpr (!Cfg::kTcRowSum) {
+      red_sum[grp * 128 + r] = l_run;
+      named_barrier_sync(1, kAttnSoftmaxThreads);
+      l_tot = l_run + red_sum[(grp ^ 1) * 128 + r];
+    }
     const float inv = l_tot > 0.f ? 1.0f / l_tot : 0.f;
     if (query < p.S) {
       uint4* dst = reinterpret_cast<uint4*>(p.ctx + static_cast<int64_t>(row_base + query) * p.ld_ctx + h * HD +
@@ -402,6 +429,8 @@ static cudaError_t launch_attention_t(const CUtensorMap& tm, const AttnParams& p
   return cudaGetLastError();
 }
 
+static cudaError_t launch_attention_pair(const CUtensorMap& tm, const AttnParams& p, cudaStream_t stream);
+
 cudaError_t launch_attention(const __nv_bfloat16* qkv, int64_t ld_qkv, int64_t q_col, int64_t k_col, int64_t v_col,
                              int64_t B, int64_t S, int64_t H, int64_t hd, const int32_t* kv_len, int causal,
                              float scale, __nv_bfloat16* ctx, int64_t ld_ctx, cudaStream_t stream) {
@@ -422,7 +451,7 @@ cudaError_t launch_attention(const __nv_bfloat16* qkv, int64_t ld_qkv, int64_t q
   p.causal = causal;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.n_q_tiles = static_cast<int>((S + 127) / 128);
-  if (hd == 64) return launch_attention_t<64>(tm, p, stream);
+  if (hd == 64) return launch_attention_pair(tm, p, stream);
   if (hd == 128) return launch_attention_t<128>(tm, p, stream);
   return cudaErrorInvalidValue;
 }

@@ -1,0 +1,388 @@
+// Flash attention forward for head_dim 64 with two query tiles per CTA (the paths of
+// BaselineSelfAttention.forward, transformer_benchmark/models.py:55-75; masks as in
+// attention.cuh).
+//
+// Why a separate kernel for head_dim 64: a 128x128 score tile costs the tensor core 2 x 128x128x64
+// MACs (S = Q K^T and O = P V, ~512 clocks) but costs the exponential unit 16384 ex2 (~1024 clocks
+// at 16/clk/SM), so the softmax, not the MMA, sets the pace. With one query tile per CTA every
+// softmax warp waits through the same latency phases (TMEM loads, row maximum, wait for the next
+// S) at the same time and the exponential unit idles. Here each CTA owns query tiles 2c and 2c+1
+// with two independent 4-warp softmax groups; each thread owns one whole query row (no exchange
+// between warps), so one group's exponentials run while the other group waits, and the tensor core
+// alternates between the groups.
+//
+// CTA = (b, h, query-tile pair c), 10 warps:
+//   warp 0      TMA: Q tiles 2c, 2c+1 once; K_j and V_j (128 keys) into 2-stage rings.
+//   warp 1      TMEM allocator and UMMA issuer. Per group t: S_t(j) = Q_t K_j^T into TMEM score
+//               buffer t; O_t(j) = P_t(j) [V_j | 1] (N = 64 + 16) into TMEM output buffer t; the
+//               ones block after each V stage makes columns 64..79 of O_t(j) the row sums of
+//               P_t(j). After group t publishes P_t(j) it issues S_t(j+1) then O_t(j).
+//   warps 2..5  softmax group 0 (query tile 2c), warps 6..9 group 1 (tile 2c+1); warp % 4 is the
+//               TMEM lane quadrant = 32 query rows. Per KV tile: pass 1 reads the 128 scores of the
+//               row from TMEM for the row maximum; then O_t(j-1) is folded into the register
+//               accumulator with the running-max correction (that frees P_t and O_t); pass 2
+//               re-reads the scores, writes unnormalised probabilities as bf16 into P_t (K-major,
+//               128-byte swizzle, the layout the P V MMA reads) and signals p_full_t, which also
+//               tells the MMA warp that S_t and O_t may be overwritten.
+#pragma once
+#include "b2_common.cuh"
+
+namespace b2 {
+
+struct AttnPairCfg {
+  static constexpr int kThreads = 320;
+  static constexpr int kBoxBytes = 128 * 128;          // 128 rows x 64 bf16 columns
+  static constexpr int kQBytes = kBoxBytes;            // one 128 x 64 query tile
+  static constexpr int kKBytes = kBoxBytes;
+  static constexpr int kVStageBytes = 2 * kBoxBytes;   // V tile + block of ones
+  static constexpr int kPBytes = 2 * kBoxBytes;        // 128 rows x 128 keys bf16
+  static constexpr int kStages = 2;
+  static constexpr int kOffQ = 0;                                   // [2]
+  static constexpr int kOffK = kOffQ + 2 * kQBytes;                 // [kStages]
+  static constexpr int kOffV = kOffK + kStages * kKBytes;           // [kStages]
+  static constexpr int kOffP = kOffV + kStages * kVStageBytes;      // [2 groups]
+  static constexpr int kOffBar = kOffP + 2 * kPBytes;
+  static constexpr int kSmemBytes = kOffBar + 256 + 1024;
+  static constexpr int kTmemCols = 512;
+  static constexpr int kSCol = 0;      // S_t at t * 128
+  static constexpr int kOCol = 256;    // O_t at 256 + t * 128 (80 columns used)
+  static constexpr int kON = 80;       // P V MMA N: 64 output columns + 16 row-sum columns
+};
+
+// Row maximum of 32 values as a balanced tree of 3-input maxima (short dependency chains).
+__device__ __forceinline__ float max32(const float* v) {
+  float a[11];
+#pragma unroll
+  for (int i = 0; i < 10; ++i) a[i] = max3f(v[3 * i], v[3 * i + 1], v[3 * i + 2]);
+  a[10] = fmaxf(v[30], v[31]);
+  const float b0 = max3f(a[0], a[1], a[2]);
+  const float b1 = max3f(a[3], a[4], a[5]);
+  const float b2 = max3f(a[6], a[7], a[8]);
+  const float b3 = fmaxf(a[9], a[10]);
+  return fmaxf(max3f(b0, b1, b2), b3);
+}
+
+__global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
+    attention_pair_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnParams p) {
+  using Cfg = AttnPairCfg;
+  constexpr int HD = 64;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* s_q = smem + Cfg::kOffQ;
+  uint8_t* s_k = smem + Cfg::kOffK;
+  uint8_t* s_v = smem + Cfg::kOffV;
+  uint8_t* s_p = smem + Cfg::kOffP;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* k_empty = bars + 3;  // [2]
+  uint64_t* v_full = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;  // [2]
+  uint64_t* s_full = bars + 9;   // [2 groups]
+  uint64_t* p_full = bars + 11;  // [2 groups]
+  uint64_t* o_full = bars + 13;  // [2 groups]
+  uint64_t* drain = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int b = blockIdx.x / p.H;
+  const int h = blockIdx.x % p.H;
+  const int n_pairs = (p.n_q_tiles + 1) >> 1;
+  const int pair = n_pairs - 1 - static_cast<int>(blockIdx.y);  // heaviest causal pairs first
+  const int kv_len = p.kv_len != nullptr ? p.kv_len[b] : p.S;
+  const int kv_tiles = (kv_len + 127) >> 7;
+  int n_kv[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int qt = 2 * pair + t;
+    const bool live = qt < p.n_q_tiles && qt * 128 < kv_len;
+    n_kv[t] = live ? (p.causal ? min(qt + 1, kv_tiles) : kv_tiles) : 0;
+  }
+  const int n_total = max(n_kv[0], n_kv[1]);
+  if (n_total == 0) return;  // uniform for the CTA: nothing allocated yet
+  const int row_base = b * p.S;
+  const int q_row0 = row_base + pair * 256;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_full[i], 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) tma_prefetch_desc(&tm_qkv);
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  for (int st = 0; st < Cfg::kStages; ++st) {
+    uint4* ones = reinterpret_cast<uint4*>(s_v + st * Cfg::kVStageBytes + Cfg::kBoxBytes);
+    for (int i = threadIdx.x; i < Cfg::kBoxBytes / 16; i += Cfg::kThreads)
+      ones[i] = make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
+  }
+  fence_proxy_async_smem();
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      const int qc = p.q_col + h * HD;
+      const int kc = p.k_col + h * HD;
+      const int vc = p.v_col + h * HD;
+      mbar_arrive_expect_tx(q_full, 2 * Cfg::kQBytes);
+      tma_load_2d(s_q, &tm_qkv, q_full, qc, q_row0);
+      tma_load_2d(s_q + Cfg::kQBytes, &tm_qkv, q_full, qc, q_row0 + 128);
+      int issued_k = 0, issued_v = 0;
+      bool ok = true;
+      for (int j = 0; j < n_total; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        const int krow = row_base + j * 128;
+        if (!mbar_wait(&k_empty[st], ph ^ 1u, abort_flag, kKernelAttention, 21)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&k_full[st], Cfg::kKBytes);
+        tma_load_2d(s_k + st * Cfg::kKBytes, &tm_qkv, &k_full[st], kc, krow);
+        ++issued_k;
+        if (!mbar_wait(&v_empty[st], ph ^ 1u, abort_flag, kKernelAttention, 22)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&v_full[st], Cfg::kBoxBytes);
+        tma_load_2d(s_v + st * Cfg::kVStageBytes, &tm_qkv, &v_full[st], vc, krow);
+        ++issued_v;
+      }
+      if (!ok) {
+        const uint64_t t0 = global_timer_ns();
+        auto drain_wait = [&](uint64_t* bar, uint32_t par) {
+          while (!mbar_try_wait(bar, par) && global_timer_ns() - t0 < kWaitTimeoutNs) {
+          }
+        };
+        drain_wait(q_full, 0);
+        for (int j = issued_k - 1; j >= 0 && j >= issued_k - 2; --j) drain_wait(&k_full[j & 1], (j >> 1) & 1);
+        for (int j = issued_v - 1; j >= 0 && j >= issued_v - 2; --j) drain_wait(&v_full[j & 1], (j >> 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- UMMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = make_idesc_bf16_f32(128, 128, 0, 0);
+      constexpr uint32_t idesc_o = make_idesc_bf16_f32(128, Cfg::kON, 0, 1);
+      const uint32_t q_addr = smem_u32(s_q);
+      auto issue_s = [&](int t, int j) {
+        const uint32_t k_addr = smem_u32(s_k + (j & 1) * Cfg::kKBytes);
+        const uint32_t a0 = q_addr + t * Cfg::kQBytes;
+        const uint32_t d = tmem_base + Cfg::kSCol + t * 128;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk)
+          umma_bf16_ss(d, make_sdesc_sw128(a0 + kk * 32, 16, 1024), make_sdesc_sw128(k_addr + kk * 32, 16, 1024),
+                       idesc_s, kk > 0 ? 1u : 0u);
+        umma_commit(&s_full[t]);
+      };
+      auto issue_o = [&](int t, int j) {
+        const uint32_t p_addr = smem_u32(s_p + t * Cfg::kPBytes);
+        const uint32_t v_addr = smem_u32(s_v + (j & 1) * Cfg::kVStageBytes);
+        const uint32_t d = tmem_base + Cfg::kOCol + t * 128;
+#pragma unroll
+        for (int kk = 0; kk < 128 / 16; ++kk)
+          umma_bf16_ss(d, make_sdesc_sw128(p_addr + (kk >> 2) * Cfg::kBoxBytes + (kk & 3) * 32, 16, 1024),
+                       make_sdesc_sw128(v_addr + kk * 2048, Cfg::kBoxBytes, 1024), idesc_o, kk > 0 ? 1u : 0u);
+        umma_commit(&o_full[t]);
+      };
+      bool ok = mbar_wait(q_full, 0, abort_flag, kKernelAttention, 23) &&
+                mbar_wait(&k_full[0], 0, abort_flag, kKernelAttention, 24);
+      if (ok) {
+        tc_fence_after_sync();
+        for (int t = 0; t < 2; ++t)
+          if (n_kv[t] > 0) issue_s(t, 0);
+        umma_commit(&k_empty[0]);
+      }
+      for (int j = 0; j < n_total && ok; ++j) {
+        bool k_next_ready = false, v_ready = false;
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (j >= n_kv[t]) continue;
+          // Group t is done with S_t(j) and O_t(j-1), and P_t(j) is in shared memory.
+          if (!mbar_wait(&p_full[t], j & 1, abort_flag, kKernelAttention, 25)) {
+            ok = false;
+            break;
+          }
+          if (j + 1 < n_kv[t]) {
+            if (!k_next_ready) {
+              if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, kKernelAttention, 26)) {
+                ok = false;
+                break;
+              }
+              k_next_ready = true;
+            }
+            tc_fence_after_sync();
+            issue_s(t, j + 1);
+            if (t == 1 || n_kv[1] <= j + 1) umma_commit(&k_empty[(j + 1) & 1]);  // last reader of K_{j+1}
+          }
+          if (!v_ready) {
+            if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1, abort_flag, kKernelAttention, 27)) {
+              ok = false;
+              break;
+            }
+            v_ready = true;
+          }
+          tc_fence_after_sync();
+          issue_o(t, j);
+          if (t == 1 || n_kv[1] <= j) umma_commit(&v_empty[j & 1]);  // last reader of V_j
+        }
+      }
+      umma_commit(drain);
+      const uint64_t t0 = global_timer_ns();
+      while (!mbar_try_wait(drain, 0) && global_timer_ns() - t0 < kWaitTimeoutNs) {
+      }
+    }
+  } else {
+    // ---------------- softmax groups ----------------
+    const int grp = (warp - 2) >> 2;
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const int qt = 2 * pair + grp;
+    const int query = qt * 128 + r;
+    const int n = n_kv[grp];
+    const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+    const uint32_t t_s = t_lane + Cfg::kSCol + grp * 128;
+    const uint32_t t_o = t_lane + Cfg::kOCol + grp * 128;
+    uint8_t* prow = s_p + grp * Cfg::kPBytes + (r >> 3) * 1024 + (r & 7) * 128;
+    const float c = p.scale_log2;
+    const int limit = p.causal ? min(kv_len, query + 1) : kv_len;
+
+    float o_acc[HD];
+#pragma unroll
+    for (int k = 0; k < HD; ++k) o_acc[k] = 0.f;
+    float m_run = -INFINITY, l_acc = 0.f, alpha_prev = 0.f;
+    bool alive = true;
+
+#pragma unroll 1
+    for (int j = 0; j < n; ++j) {
+      softmax_wait(&s_full[grp], j & 1, 28, alive, abort_flag);
+      tc_fence_after_sync();
+      const bool last = j == n - 1;
+      const int n_valid = limit - j * 128;  // keys [0, n_valid) of this tile are visible (last tile)
+
+      // pass 1: row maximum
+      float rmax = -INFINITY;
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        float v[32];
+        tmem_load_32cols(t_s + cc * 32, v);
+        if (last) {
+#pragma unroll
+          for (int k = 0; k < 32; ++k) v[k] = (cc * 32 + k < n_valid) ? v[k] : -INFINITY;
+        }
+        rmax = fmaxf(rmax, max32(v));
+      }
+      const float m_new = fmaxf(m_run, rmax);
+      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+      const float alpha = fast_exp2((m_run - m_use) * c);
+      const float neg_mc = -m_use * c;
+
+      // fold O_t(j-1) into the accumulator (frees P_t and O_t for tile j)
+      if (j > 0) {
+        softmax_wait(&o_full[grp], (j - 1) & 1, 29, alive, abort_flag);
+        tc_fence_after_sync();
+        l_acc = fmaf(l_acc, alpha_prev, tmem_load_1col(t_o + HD));
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          float v[32];
+          tmem_load_32cols(t_o + cc * 32, v);
+#pragma unroll
+          for (int k = 0; k < 32; ++k) o_acc[cc * 32 + k] = fmaf(o_acc[cc * 32 + k], alpha_prev, v[k]);
+        }
+      }
+
+      // pass 2: probabilities -> P_t (row r, keys 32cc..32cc+31 = 16-byte chunks 4(cc%2)..+3 of atom cc/2)
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        float v[32];
+        tmem_load_32cols(t_s + cc * 32, v);
+        if (last) {
+#pragma unroll
+          for (int k = 0; k < 32; ++k) v[k] = (cc * 32 + k < n_valid) ? v[k] : -INFINITY;
+        }
+        uint8_t* patom = prow + (cc >> 1) * Cfg::kBoxBytes;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t w[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float e0 = fast_exp2(fmaf(v[8 * q + 2 * k], c, neg_mc));
+            const float e1 = fast_exp2(fmaf(v[8 * q + 2 * k + 1], c, neg_mc));
+            w[k] = pack_bf16x2(e0, e1);
+          }
+          const int chunk = (cc & 1) * 4 + q;
+          *reinterpret_cast<uint4*>(patom + ((chunk ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      m_run = m_new;
+      alpha_prev = alpha;
+      fence_proxy_async_smem();
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[grp]);
+    }
+
+    if (n > 0) {
+      softmax_wait(&o_full[grp], (n - 1) & 1, 30, alive, abort_flag);
+      tc_fence_after_sync();
+      l_acc = fmaf(l_acc, alpha_prev, tmem_load_1col(t_o + HD));
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        float v[32];
+        tmem_load_32cols(t_o + cc * 32, v);
+#pragma unroll
+        for (int k = 0; k < 32; ++k) o_acc[cc * 32 + k] = fmaf(o_acc[cc * 32 + k], alpha_prev, v[k]);
+      }
+      const float inv = l_acc > 0.f ? 1.0f / l_acc : 0.f;
+      if (query < p.S) {
+        uint4* dst = reinterpret_cast<uint4*>(p.ctx + static_cast<int64_t>(row_base + query) * p.ld_ctx + h * HD);
+#pragma unroll
+        for (int v = 0; v < HD / 8; ++v)
+          dst[v] = make_uint4(pack_bf16x2(o_acc[8 * v] * inv, o_acc[8 * v + 1] * inv),
+                              pack_bf16x2(o_acc[8 * v + 2] * inv, o_acc[8 * v + 3] * inv),
+                              pack_bf16x2(o_acc[8 * v + 4] * inv, o_acc[8 * v + 5] * inv),
+                              pack_bf16x2(o_acc[8 * v + 6] * inv, o_acc[8 * v + 7] * inv));
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+static cudaError_t launch_attention_pair(const CUtensorMap& tm, const AttnParams& p, cudaStream_t stream) {
+  static std::once_flag once[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaError_t attr_err = cudaSuccess;
+  std::call_once(once[dev & 63], [&] {
+    attr_err = cudaFuncSetAttribute(attention_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    AttnPairCfg::kSmemBytes);
+  });
+  if (attr_err != cudaSuccess) return attr_err;
+  dim3 grid(p.B * p.H, (p.n_q_tiles + 1) / 2);
+  attention_pair_kernel<<<grid, AttnPairCfg::kThreads, AttnPairCfg::kSmemBytes, stream>>>(tm, p);
+  return cudaGetLastError();
+}
+
+}  // namespace b2

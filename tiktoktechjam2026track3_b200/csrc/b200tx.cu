@@ -19,6 +19,7 @@
 #include "layernorm.cuh"
 #include "gemm.cuh"
 #include "attention.cuh"
+#include "attention_pair.cuh"
 
 #define B2_API extern "C" __attribute__((visibility("default")))
 

@@ -207,6 +207,19 @@ __device__ __forceinline__ void tmem_load_32cols(uint32_t taddr, float* v) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// One fp32 column of this thread's TMEM lane (same convergence and wait rules as above).
+__device__ __forceinline__ float tmem_load_1col(uint32_t taddr) {
+  uint32_t r;
+  __syncwarp();
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];\n\t"
+      "tcgen05.wait::ld.sync.aligned;\n"
+      : "=r"(r)
+      : "r"(taddr)
+      : "memory");
+  return __uint_as_float(r);
+}
+
 // ---------------------------------------------------------------------------------------------
 // Descriptors
 // ---------------------------------------------------------------------------------------------
@@ -249,6 +262,12 @@ __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(_
 
 // Exact (erf-based) GELU, the form torch.nn.functional.gelu(approximate="none") computes.
 __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f)); }
+
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
 
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;

@@ -16,8 +16,9 @@
 //   warp 0      TMA producer: A tile 128x64 and W tile BNx64 per k-block into a kStages ring.
 //   warp 1      TMEM allocator and single-thread UMMA issuer (128xBNx16 per instruction);
 //               tcgen05.commit frees smem stages and publishes finished accumulators.
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator rows owned by the warp's TMEM lane
-//               quadrant, fused pointwise op, stores to global memory.
+//   warps 2..9  epilogue: tcgen05.ld of the accumulator rows owned by the warp's TMEM lane
+//               quadrant (two warps per quadrant, one per half of the columns), fused pointwise
+//               op, stores to global memory.
 // Two TMEM accumulators (2 x BN fp32 columns) let the epilogue of tile i overlap the main loop
 // of tile i+1.
 #include <mutex>
@@ -46,7 +47,8 @@ struct GemmParams {
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;
-constexpr int kGemmThreads = 192;
+constexpr int kGemmThreads = 320;
+constexpr int kGemmEpilogueThreads = 256;
 
 template <int BN>
 struct GemmCfg {
@@ -161,7 +163,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 128);
+      mbar_init(&acc_empty[b], kGemmEpilogueThreads);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -264,7 +266,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_drain_wait(drain, 0);
     }
   } else {
+    // Two warps per TMEM lane quadrant; each covers one half of the tile's columns.
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row_in_tile = quad * 32 + lane;
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
@@ -277,7 +281,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int row = m_blk * kGemmBM + row_in_tile;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
         const int col0 = n_blk * BN + c * 32;
         if (col0 >= p.N) break;  // warp-uniform
         float v[32];

@@ -134,6 +134,10 @@ class UserOptimizedTransformer(nn.Module):
         self._packed_key: Optional[tuple] = None
         self._mask_lengths = MaskLengths()
         self._launch_log: Optional[list] = None
+        # CUDA-graph replay of the per-block launches (launch amortisation only: the graph holds
+        # exactly the kernels the eager path launches). Keyed by shape, device and mask presence.
+        self.use_cuda_graph = True
+        self._graphs: Dict[tuple, "_GraphedStack"] = {}
 
     # ------------------------------------------------------------------ weights
     def _weights_key(self) -> tuple:
@@ -224,37 +228,101 @@ class UserOptimizedTransformer(nn.Module):
         packed: List[_PackedBlock],
     ) -> torch.Tensor:
         cfg = self.config
-        d, f, h, hd = cfg.d_model, cfg.ffn_dim, cfg.num_heads, cfg.head_dim
-        tokens = batch * seq_len
-        dev = x.device
-        resid = torch.empty(tokens, d, device=dev, dtype=torch.float32)
-        ln = torch.empty(tokens, d, device=dev, dtype=torch.bfloat16)
-        qkv = torch.empty(tokens, 3 * d, device=dev, dtype=torch.bfloat16)
-        ctx = torch.empty(tokens, d, device=dev, dtype=torch.bfloat16)
-        hidden = torch.empty(tokens, f, device=dev, dtype=torch.bfloat16)
-        out = torch.empty(batch, seq_len, d, device=dev, dtype=torch.bfloat16)
-        x2 = x.view(tokens, d)
+        tokens, d = batch * seq_len, cfg.d_model
+        out = torch.empty(batch, seq_len, d, device=x.device, dtype=torch.bfloat16)
+        if self.use_cuda_graph and self._launch_log is None:
+            shape_key = (batch, seq_len, x.device, kv_len is not None)
+            stack = self._graphs.get(shape_key)
+            if stack is None or stack.packed is not packed:  # new shape, or weights changed: (re)capture
+                self._graphs.pop(shape_key, None)
+                stack = _GraphedStack(self, batch, seq_len, x.device, kv_len is not None, packed)
+                self._graphs[shape_key] = stack
+            stack.run(x.view(tokens, d), kv_len, row_mask, out.view(tokens, d))
+            return out
+        ws = _Workspace(cfg, batch, seq_len, x.device)
+        pb0 = packed[0]
+        self._timed("layernorm", _capi.layernorm, x.view(tokens, d), pb0.ln1_w, pb0.ln1_b, pb0.ln1_eps, ws.ln,
+                    resid_out=ws.resid)
+        self._blocks(ws, batch, seq_len, kv_len, row_mask, packed)
+        fn = self.final_norm
+        self._timed("layernorm", _capi.layernorm, ws.resid, fn.weight, fn.bias, float(fn.eps), out.view(tokens, d),
+                    row_mask=row_mask)
+        return out
+
+    def _blocks(self, ws: "_Workspace", batch: int, seq_len: int, kv_len, row_mask, packed) -> None:
+        """Every launch between the first LayerNorm (done) and the final LayerNorm."""
+        cfg = self.config
+        d, h, hd = cfg.d_model, cfg.num_heads, cfg.head_dim
         scale = hd**-0.5
         t = self._timed
         for i, pb in enumerate(packed):
-            if i == 0:
-                t("layernorm", _capi.layernorm, x2, pb.ln1_w, pb.ln1_b, pb.ln1_eps, ln, resid_out=resid)
-            else:
-                t("layernorm", _capi.layernorm, resid, pb.ln1_w, pb.ln1_b, pb.ln1_eps, ln)
-            t("gemm_qkv", _capi.linear, ln, pb.w_qkv, pb.b_qkv, _capi.EPI_BIAS, qkv)
-            t("attention", _capi.attention, qkv, batch, seq_len, h, hd, 0, d, 2 * d, kv_len, cfg.causal, scale, ctx)
-            t("gemm_out", _capi.linear, ctx, pb.w_o, pb.b_o, _capi.EPI_RESIDUAL, resid, row_mask)
-            t("layernorm", _capi.layernorm, resid, pb.ln2_w, pb.ln2_b, pb.ln2_eps, ln)
-            t("gemm_ffn_in", _capi.linear, ln, pb.w_1, pb.b_1, _capi.EPI_BIAS_GELU, hidden)
-            t("gemm_ffn_out", _capi.linear, hidden, pb.w_2, pb.b_2, _capi.EPI_RESIDUAL_ZERO, resid, row_mask)
-        fn = self.final_norm
-        t("layernorm", _capi.layernorm, resid, fn.weight, fn.bias, float(fn.eps), out.view(tokens, d),
-          row_mask=row_mask)
-        return out
+            if i > 0:
+                t("layernorm", _capi.layernorm, ws.resid, pb.ln1_w, pb.ln1_b, pb.ln1_eps, ws.ln)
+            t("gemm_qkv", _capi.linear, ws.ln, pb.w_qkv, pb.b_qkv, _capi.EPI_BIAS, ws.qkv)
+            t("attention", _capi.attention, ws.qkv, batch, seq_len, h, hd, 0, d, 2 * d, kv_len, cfg.causal, scale,
+              ws.ctx)
+            t("gemm_out", _capi.linear, ws.ctx, pb.w_o, pb.b_o, _capi.EPI_RESIDUAL, ws.resid, row_mask)
+            t("layernorm", _capi.layernorm, ws.resid, pb.ln2_w, pb.ln2_b, pb.ln2_eps, ws.ln)
+            t("gemm_ffn_in", _capi.linear, ws.ln, pb.w_1, pb.b_1, _capi.EPI_BIAS_GELU, ws.hidden)
+            t("gemm_ffn_out", _capi.linear, ws.hidden, pb.w_2, pb.b_2, _capi.EPI_RESIDUAL_ZERO, ws.resid, row_mask)
+
+    def release_graphs(self) -> None:
+        """Drops captured CUDA graphs and their static buffers."""
+        self._graphs.clear()
 
     @staticmethod
     def launches_per_forward(num_layers: int) -> int:
         return 7 * num_layers + 1
+
+
+class _Workspace:
+    """Activation buffers of one forward pass (token-major, T = B*S rows)."""
+
+    def __init__(self, cfg: TransformerConfig, batch: int, seq_len: int, device: torch.device) -> None:
+        tokens, d, f = batch * seq_len, cfg.d_model, cfg.ffn_dim
+        self.resid = torch.empty(tokens, d, device=device, dtype=torch.float32)
+        self.ln = torch.empty(tokens, d, device=device, dtype=torch.bfloat16)
+        self.qkv = torch.empty(tokens, 3 * d, device=device, dtype=torch.bfloat16)
+        self.ctx = torch.empty(tokens, d, device=device, dtype=torch.bfloat16)
+        self.hidden = torch.empty(tokens, f, device=device, dtype=torch.bfloat16)
+
+
+class _GraphedStack:
+    """A CUDA graph of UserOptimizedTransformer._blocks over static buffers.
+
+    Per call: the mask-derived lengths/row mask are copied into static tensors, the first
+    LayerNorm reads the caller's x directly into the static buffers, the graph replays every
+    launch of the blocks, and the final LayerNorm writes the caller's fresh output tensor.
+    """
+
+    def __init__(self, model: "UserOptimizedTransformer", batch: int, seq_len: int, device: torch.device,
+                 masked: bool, packed: List[_PackedBlock]) -> None:
+        self.model = model
+        self.packed = packed
+        self.ws = _Workspace(model.config, batch, seq_len, device)
+        self.kv_len = torch.zeros(batch, device=device, dtype=torch.int32) if masked else None
+        self.row_mask = torch.zeros(batch * seq_len, device=device, dtype=torch.uint8) if masked else None
+        self.ws.resid.zero_()
+        self.ws.ln.zero_()
+        if masked:
+            self.kv_len.fill_(seq_len)
+            self.row_mask.fill_(1)
+        # One eager pass (first use of each kernel sets its attributes outside capture), then capture.
+        model._blocks(self.ws, batch, seq_len, self.kv_len, self.row_mask, packed)
+        torch.cuda.current_stream(device).synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            model._blocks(self.ws, batch, seq_len, self.kv_len, self.row_mask, packed)
+
+    def run(self, x2: torch.Tensor, kv_len, row_mask, out2: torch.Tensor) -> None:
+        if self.kv_len is not None:
+            self.kv_len.copy_(kv_len)
+            self.row_mask.copy_(row_mask)
+        pb0 = self.packed[0]
+        _capi.layernorm(x2, pb0.ln1_w, pb0.ln1_b, pb0.ln1_eps, self.ws.ln, resid_out=self.ws.resid)
+        self.graph.replay()
+        fn = self.model.final_norm
+        _capi.layernorm(self.ws.resid, fn.weight, fn.bias, float(fn.eps), out2, row_mask=self.row_mask)
 
 
 def copy_model_weights(baseline: nn.Module, optimized: nn.Module, strict: bool = True) -> None:
