@@ -86,7 +86,7 @@ int b2_add_layernorm_fwd(float* resid, const float* delta, const void* bias, con
  *   a    [m, k] bf16;  w [n, k] bf16 (nn.Linear weight layout);  bias [n] bf16 or NULL
  *   out  [m, ldo] bf16 (B2_EPI_BIAS, B2_EPI_BIAS_GELU) or fp32 (others)
  *   row_mask [m] uint8 or NULL (residual epilogues only)
- *   tile_n 0 = choose, or 128 / 256
+ *   tile_n 0 = choose, or 128 / 192 / 256 (192 and 256 need n to be a multiple)
  * Requires n % 32 == 0, k % 8 == 0, ldo % 8 == 0, 16-byte aligned pointers, an sm_100 device.
  */
 int b2_linear_fwd(const void* a, const void* w, const void* bias, int64_t m, int64_t n, int64_t k, int epilogue,

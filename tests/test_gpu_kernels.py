@@ -60,6 +60,7 @@ def test_layernorm_bf16_input_writes_residual_and_masks_rows(d):
 # ---------------------------------------------------------------------------------- GEMM
 GEMM_SHAPES = [
     (128, 256, 64),
+    (4096, 768, 768),    # C2 out_proj (128x192 tiles)
     (200, 384, 200),     # ragged M and K, N not a multiple of 256
     (4096, 2304, 768),   # C2 packed QKV
     (1000, 3072, 768),   # C2 ffn_in, ragged M
@@ -115,10 +116,11 @@ def test_gemm_store_f32_and_tile_choice_agree(m, n, k):
     out128 = torch.empty(m, n, device="cuda")
     _capi.linear(a, w, None, _capi.EPI_STORE_F32, out128, tile_n=128)
     torch.testing.assert_close(out128, ref - bias.float(), atol=2e-3, rtol=1e-4)
-    if n % 256 == 0:
-        out256 = torch.empty(m, n, device="cuda")
-        _capi.linear(a, w, None, _capi.EPI_STORE_F32, out256, tile_n=256)
-        assert torch.equal(out128, out256)
+    for tile in (192, 256):
+        if n % tile == 0:
+            other = torch.empty(m, n, device="cuda")
+            _capi.linear(a, w, None, _capi.EPI_STORE_F32, other, tile_n=tile)
+            assert torch.equal(out128, other), tile
 
 
 def test_gemm_is_row_invariant():

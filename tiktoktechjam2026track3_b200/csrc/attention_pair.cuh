@@ -14,16 +14,19 @@
 // CTA = (b, h, query-tile pair c), 10 warps:
 //   warp 0      TMA: Q tiles 2c, 2c+1 once; K_j and V_j (128 keys) into 2-stage rings.
 //   warp 1      TMEM allocator and UMMA issuer. Per group t: S_t(j) = Q_t K_j^T into TMEM score
-//               buffer t; O_t(j) = P_t(j) [V_j | 1] (N = 64 + 16) into TMEM output buffer t; the
-//               ones block after each V stage makes columns 64..79 of O_t(j) the row sums of
-//               P_t(j). After group t publishes P_t(j) it issues S_t(j+1) then O_t(j).
+//               buffer t; O_t += P_t(j) [V_j | 1] (N = 64 + 16) accumulated in TMEM output buffer
+//               t across all KV tiles; the ones block after each V stage makes columns 64..79 of
+//               O_t the running row sums of P. After group t publishes P_t(j) it issues S_t(j+1)
+//               then the P_t(j) V_j accumulation.
 //   warps 2..5  softmax group 0 (query tile 2c), warps 6..9 group 1 (tile 2c+1); warp % 4 is the
-//               TMEM lane quadrant = 32 query rows. Per KV tile: pass 1 reads the 128 scores of the
-//               row from TMEM for the row maximum; then O_t(j-1) is folded into the register
-//               accumulator with the running-max correction (that frees P_t and O_t); pass 2
-//               re-reads the scores, writes unnormalised probabilities as bf16 into P_t (K-major,
-//               128-byte swizzle, the layout the P V MMA reads) and signals p_full_t, which also
-//               tells the MMA warp that S_t and O_t may be overwritten.
+//               TMEM lane quadrant = 32 query rows. Per KV tile a thread loads its row's 128 scores
+//               from TMEM, takes the row maximum, writes exp2(c*s - c*m) as bf16 into P_t
+//               (K-major, 128-byte swizzle, the layout the P V MMA reads) and signals p_full_t,
+//               which also tells the MMA warp that S_t may be overwritten. The reference maximum m
+//               of a row only moves when the tile maximum exceeds it by more than 2^8 in exp2
+//               units (probabilities up to 256 are exact enough in bf16/fp32); then, and only then,
+//               the warp waits for the previous accumulation and rescales its O_t rows (output and
+//               row-sum columns together) in TMEM. The final 1/l comes from the row-sum column.
 #pragma once
 #include "b2_common.cuh"
 
@@ -200,7 +203,8 @@ __global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < 128 / 16; ++kk)
           umma_bf16_ss(d, make_sdesc_sw128(p_addr + (kk >> 2) * Cfg::kBoxBytes + (kk & 3) * 32, 16, 1024),
-                       make_sdesc_sw128(v_addr + kk * 2048, Cfg::kBoxBytes, 1024), idesc_o, kk > 0 ? 1u : 0u);
+                       make_sdesc_sw128(v_addr + kk * 2048, Cfg::kBoxBytes, 1024), idesc_o,
+                       (j > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&o_full[t]);
       };
       bool ok = mbar_wait(q_full, 0, abort_flag, kKernelAttention, 23) &&
@@ -256,83 +260,67 @@ __global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
     const int r = quad * 32 + lane;
     const int qt = 2 * pair + grp;
     const int query = qt * 128 + r;
-    const int n = n_kv[grp];
+    const int n = grp == 0 ? n_kv[0] : n_kv[1];
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
     const uint32_t t_s = t_lane + Cfg::kSCol + grp * 128;
     const uint32_t t_o = t_lane + Cfg::kOCol + grp * 128;
     uint8_t* prow = s_p + grp * Cfg::kPBytes + (r >> 3) * 1024 + (r & 7) * 128;
     const float c = p.scale_log2;
     const int limit = p.causal ? min(kv_len, query + 1) : kv_len;
+    constexpr float kRescaleThreshold = 8.0f;  // exp2 units: rescale only when m grows by > 2^8
 
-    float o_acc[HD];
-#pragma unroll
-    for (int k = 0; k < HD; ++k) o_acc[k] = 0.f;
-    float m_run = -INFINITY, l_acc = 0.f, alpha_prev = 0.f;
+    float m_ref = 0.f;  // reference maximum (raw score units) used in exp2(c * (s - m_ref))
     bool alive = true;
 
 #pragma unroll 1
     for (int j = 0; j < n; ++j) {
       softmax_wait(&s_full[grp], j & 1, 28, alive, abort_flag);
       tc_fence_after_sync();
-      const bool last = j == n - 1;
-      const int n_valid = limit - j * 128;  // keys [0, n_valid) of this tile are visible (last tile)
-
-      // pass 1: row maximum
-      float rmax = -INFINITY;
+      float v[128];
+      tmem_load_128cols(t_s, v);
+      if (j == n - 1) {
+        const int n_valid = limit - j * 128;  // keys [0, n_valid) of the last tile are visible
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        float v[32];
-        tmem_load_32cols(t_s + cc * 32, v);
-        if (last) {
-#pragma unroll
-          for (int k = 0; k < 32; ++k) v[k] = (cc * 32 + k < n_valid) ? v[k] : -INFINITY;
-        }
-        rmax = fmaxf(rmax, max32(v));
+        for (int k = 0; k < 128; ++k) v[k] = (k < n_valid) ? v[k] : -INFINITY;
       }
-      const float m_new = fmaxf(m_run, rmax);
-      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-      const float alpha = fast_exp2((m_run - m_use) * c);
-      const float neg_mc = -m_use * c;
-
-      // fold O_t(j-1) into the accumulator (frees P_t and O_t for tile j)
-      if (j > 0) {
+      const float rmax = fmaxf(fmaxf(max32(v), max32(v + 32)), fmaxf(max32(v + 64), max32(v + 96)));
+      float alpha = 1.f;  // < 1 when this row's reference maximum moves (rare after the first tile)
+      if (j == 0) {
+        m_ref = rmax == -INFINITY ? 0.f : rmax;
+      } else if ((rmax - m_ref) * c > kRescaleThreshold) {
+        alpha = fast_exp2((m_ref - rmax) * c);
+        m_ref = rmax;
+      }
+      const float neg_mc = -m_ref * c;
+      // probabilities -> P_t: row r, keys 8q..8q+7 = 16-byte chunk (q % 8) of atom q / 8
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        uint32_t w[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float e0 = fast_exp2(fmaf(v[8 * q + 2 * k], c, neg_mc));
+          const float e1 = fast_exp2(fmaf(v[8 * q + 2 * k + 1], c, neg_mc));
+          w[k] = pack_bf16x2(e0, e1);
+        }
+        *reinterpret_cast<uint4*>(prow + (q >> 3) * Cfg::kBoxBytes + (((q & 7) ^ (r & 7)) << 4)) =
+            make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      if (__any_sync(0xffffffffu, alpha < 1.f)) {
+        // Rescale the accumulated output and row sums (P_t(0..j-1) V) of the warp's rows to their
+        // new reference maxima (alpha = 1 for rows whose maximum did not move) once the
+        // accumulation of tile j-1 has landed, before P_t(j) V is accumulated. Warp-uniform: the
+        // TMEM loads and stores are warp-collective.
         softmax_wait(&o_full[grp], (j - 1) & 1, 29, alive, abort_flag);
         tc_fence_after_sync();
-        l_acc = fmaf(l_acc, alpha_prev, tmem_load_1col(t_o + HD));
+#pragma unroll 1
+        for (int cc = 0; cc < 3; ++cc) {
+          float o[32];
+          tmem_load_32cols(t_o + cc * 32, o);
 #pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-          float v[32];
-          tmem_load_32cols(t_o + cc * 32, v);
-#pragma unroll
-          for (int k = 0; k < 32; ++k) o_acc[cc * 32 + k] = fmaf(o_acc[cc * 32 + k], alpha_prev, v[k]);
+          for (int k = 0; k < 32; ++k) o[k] *= alpha;
+          tmem_store_32cols(t_o + cc * 32, o);
         }
       }
-
-      // pass 2: probabilities -> P_t (row r, keys 32cc..32cc+31 = 16-byte chunks 4(cc%2)..+3 of atom cc/2)
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        float v[32];
-        tmem_load_32cols(t_s + cc * 32, v);
-        if (last) {
-#pragma unroll
-          for (int k = 0; k < 32; ++k) v[k] = (cc * 32 + k < n_valid) ? v[k] : -INFINITY;
-        }
-        uint8_t* patom = prow + (cc >> 1) * Cfg::kBoxBytes;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint32_t w[4];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float e0 = fast_exp2(fmaf(v[8 * q + 2 * k], c, neg_mc));
-            const float e1 = fast_exp2(fmaf(v[8 * q + 2 * k + 1], c, neg_mc));
-            w[k] = pack_bf16x2(e0, e1);
-          }
-          const int chunk = (cc & 1) * 4 + q;
-          *reinterpret_cast<uint4*>(patom + ((chunk ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-      }
-      m_run = m_new;
-      alpha_prev = alpha;
       fence_proxy_async_smem();
       tc_fence_before_sync();
       __syncwarp();
@@ -342,23 +330,19 @@ __global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
     if (n > 0) {
       softmax_wait(&o_full[grp], (n - 1) & 1, 30, alive, abort_flag);
       tc_fence_after_sync();
-      l_acc = fmaf(l_acc, alpha_prev, tmem_load_1col(t_o + HD));
-#pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
-        float v[32];
-        tmem_load_32cols(t_o + cc * 32, v);
-#pragma unroll
-        for (int k = 0; k < 32; ++k) o_acc[cc * 32 + k] = fmaf(o_acc[cc * 32 + k], alpha_prev, v[k]);
-      }
-      const float inv = l_acc > 0.f ? 1.0f / l_acc : 0.f;
+      const float l = tmem_load_1col(t_o + HD);
+      const float inv = l > 0.f ? 1.0f / l : 0.f;
+      float o[64];
+      tmem_load_32cols(t_o, o);
+      tmem_load_32cols(t_o + 32, o + 32);
       if (query < p.S) {
         uint4* dst = reinterpret_cast<uint4*>(p.ctx + static_cast<int64_t>(row_base + query) * p.ld_ctx + h * HD);
 #pragma unroll
-        for (int v = 0; v < HD / 8; ++v)
-          dst[v] = make_uint4(pack_bf16x2(o_acc[8 * v] * inv, o_acc[8 * v + 1] * inv),
-                              pack_bf16x2(o_acc[8 * v + 2] * inv, o_acc[8 * v + 3] * inv),
-                              pack_bf16x2(o_acc[8 * v + 4] * inv, o_acc[8 * v + 5] * inv),
-                              pack_bf16x2(o_acc[8 * v + 6] * inv, o_acc[8 * v + 7] * inv));
+        for (int k = 0; k < HD / 8; ++k)
+          dst[k] = make_uint4(pack_bf16x2(o[8 * k] * inv, o[8 * k + 1] * inv),
+                              pack_bf16x2(o[8 * k + 2] * inv, o[8 * k + 3] * inv),
+                              pack_bf16x2(o[8 * k + 4] * inv, o[8 * k + 5] * inv),
+                              pack_bf16x2(o[8 * k + 6] * inv, o[8 * k + 7] * inv));
       }
     }
   }

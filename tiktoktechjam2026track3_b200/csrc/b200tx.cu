@@ -137,8 +137,10 @@ B2_API int b2_linear_fwd(const void* a, const void* w, const void* bias, int64_t
   if (n % 32 != 0) return fail(2, "b2_linear_fwd: n=%lld must be a multiple of 32", (long long)n);
   if (k % 8 != 0) return fail(2, "b2_linear_fwd: k=%lld must be a multiple of 8", (long long)k);
   if (ldo < n || ldo % 8 != 0) return fail(2, "b2_linear_fwd: ldo=%lld must be >= n and a multiple of 8", (long long)ldo);
-  if (tile_n != 0 && tile_n != 128 && tile_n != 256) return fail(1, "b2_linear_fwd: tile_n must be 0, 128 or 256");
-  if (tile_n == 256 && n % 256 != 0) return fail(2, "b2_linear_fwd: tile_n=256 needs n %% 256 == 0");
+  if (tile_n != 0 && tile_n != 128 && tile_n != 192 && tile_n != 256)
+    return fail(1, "b2_linear_fwd: tile_n must be 0, 128, 192 or 256");
+  if ((tile_n == 256 || tile_n == 192) && n % tile_n != 0)
+    return fail(2, "b2_linear_fwd: tile_n=%d needs n %% %d == 0", tile_n, tile_n);
   if (!aligned16(a) || !aligned16(w) || !aligned16(out) || (bias && !aligned16(bias)))
     return fail(2, "b2_linear_fwd: pointers must be 16-byte aligned");
   if (m > 0x7fffff00LL || n > 0x7fffff00LL) return fail(2, "b2_linear_fwd: dimension exceeds 2^31");

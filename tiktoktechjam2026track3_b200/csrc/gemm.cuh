@@ -52,11 +52,12 @@ constexpr int kGemmEpilogueThreads = 256;
 
 template <int BN>
 struct GemmCfg {
-  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kStages = BN == 256 ? 4 : (BN == 192 ? 5 : 6);
   static constexpr int kABytes = kGemmBM * kGemmBK * 2;
   static constexpr int kBBytes = BN * kGemmBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kTmemCols = 2 * BN;
+  static constexpr int kAccStride = BN == 192 ? 256 : BN;  // TMEM column distance of the 2 accumulators
+  static constexpr int kTmemCols = 2 * kAccStride;          // a power of two, as tcgen05.alloc requires
   static constexpr int kBarrierBytes = 256;
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes;
 };
@@ -237,7 +238,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           break;
         }
         tc_fence_after_sync();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Cfg::kAccStride);
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!mbar_wait(&full[s], ph, abort_flag, kKernelGemm, 3)) {
             ok = false;
@@ -279,7 +280,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!mbar_wait(&acc_full[acc], acc_ph, abort_flag, kKernelGemm, 4)) break;
       tc_fence_after_sync();
       const int row = m_blk * kGemmBM + row_in_tile;
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      const uint32_t t_row =
+          tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * Cfg::kAccStride);
 #pragma unroll 1
       for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
         const int col0 = n_blk * BN + c * 32;
@@ -343,14 +345,28 @@ static cudaError_t dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMa
   }
 }
 
-// Picks the N tile: 256 keeps the tensor core fed from shared memory with one 128-row CTA;
-// 128 is used when N is not a multiple of 256, or when 256-wide tiles leave most SMs idle.
+// Picks the N tile by the fraction of SM slots the tiles fill (waves rounded up), weighted by how
+// well each tile width keeps the tensor core fed from shared memory (128x256 best). 192 exists for
+// the D=768 projections: 768 = 4 x 192 gives one nearly full wave at M=4096 where 256 leaves a
+// third of the SMs idle.
 int gemm_pick_bn(int M, int N, int sm_count) {
-  if (N % 256 != 0) return 128;
   const long m_blocks = (M + kGemmBM - 1) / kGemmBM;
-  const long t256 = m_blocks * (N / 256);
-  if (t256 * 2 <= sm_count) return 128;
-  return 256;
+  const int candidates[3] = {256, 192, 128};
+  const double intensity[3] = {1.0, 0.97, 0.85};
+  int best = 128;
+  double best_score = -1.0;
+  for (int i = 0; i < 3; ++i) {
+    const int bn = candidates[i];
+    if (bn != 128 && N % bn != 0) continue;
+    const long tiles = m_blocks * ((N + bn - 1) / bn);
+    const long waves = (tiles + sm_count - 1) / sm_count;
+    const double score = intensity[i] * static_cast<double>(tiles) / static_cast<double>(waves * sm_count);
+    if (score > best_score + 1e-9) {
+      best = bn;
+      best_score = score;
+    }
+  }
+  return best;
 }
 
 cudaError_t launch_gemm(const __nv_bfloat16* A, const __nv_bfloat16* W, const __nv_bfloat16* bias, int64_t M,
@@ -379,6 +395,7 @@ cudaError_t launch_gemm(const __nv_bfloat16* A, const __nv_bfloat16* W, const __
   const long tiles = static_cast<long>(p.m_blocks) * p.n_blocks;
   const int grid = static_cast<int>(tiles < sms ? tiles : sms);
   if (bn == 256) return dispatch_epi<256>(epi, ta, tb, p, grid, stream);
+  if (bn == 192) return dispatch_epi<192>(epi, ta, tb, p, grid, stream);
   return dispatch_epi<128>(epi, ta, tb, p, grid, stream);
 }
 
