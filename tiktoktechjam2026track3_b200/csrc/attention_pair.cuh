@@ -11,18 +11,24 @@
 // between warps), so one group's exponentials run while the other group waits, and the tensor core
 // alternates between the groups.
 //
-// CTA = (b, h, query-tile pair c), 10 warps:
-//   warp 0      TMA: Q tiles 2c, 2c+1 once; K_j and V_j (128 keys) into 2-stage rings.
-//   warp 1      TMEM allocator and UMMA issuer. Per group t: S_t(j) = Q_t K_j^T into TMEM score
-//               buffer t; O_t += P_t(j) [V_j | 1] (N = 64 + 16) accumulated in TMEM output buffer
-//               t across all KV tiles; the ones block after each V stage makes columns 64..79 of
-//               O_t the running row sums of P. After group t publishes P_t(j) it issues S_t(j+1)
-//               then the P_t(j) V_j accumulation.
-//   warps 2..5  softmax group 0 (query tile 2c), warps 6..9 group 1 (tile 2c+1); warp % 4 is the
+// CTA = (b, h, query-tile pair c), 11 warps:
+//   warp 0      TMA: Q tiles 2c, 2c+1 once; K_j and V_j (128 keys) into two independent 3-stage
+//               rings, each refilled as soon as its own slot frees (K never waits behind V).
+//   warps 1, 2  UMMA issuers, one per softmax group (warp 1 also allocates TMEM). tcgen05.mma
+//               issue blocks the issuing thread for about the instruction's execution time, so a
+//               single issuer serving both groups would make one group's P V delay the other's
+//               next S. Issuer t: S_t(j) = Q_t K_j^T into TMEM score buffer t, issued as soon as
+//               group t has S_t(j-1) in registers (s_free_t); O_t += P_t(j) [V_j | 1] (N = 64+16)
+//               accumulated in TMEM output buffer t once P_t(j) is published (p_full_t). A block of
+//               ones, addressed as the second 64-column block of the MN-major V operand (leading
+//               byte offset = distance from the V stage), makes columns 64..79 of O_t the running
+//               row sums of P. A K/V slot is refilled after both issuers released it (a group with
+//               fewer tiles releases the rest once each slot's previous use is done).
+//   warps 3..6  softmax group 0 (query tile 2c), warps 7..10 group 1 (tile 2c+1); warp % 4 is the
 //               TMEM lane quadrant = 32 query rows. Per KV tile a thread loads its row's 128 scores
 //               from TMEM, takes the row maximum, writes exp2(c*s - c*m) as bf16 into P_t
-//               (K-major, 128-byte swizzle, the layout the P V MMA reads) and signals p_full_t,
-//               which also tells the MMA warp that S_t may be overwritten. The reference maximum m
+//               (K-major, 128-byte swizzle, the layout the P V MMA reads) once P_t(j-1) V has been
+//               accumulated (o_full_t), and signals p_full_t. The reference maximum m
 //               of a row only moves when the tile maximum exceeds it by more than 2^8 in exp2
 //               units (probabilities up to 256 are exact enough in bf16/fp32); then, and only then,
 //               the warp waits for the previous accumulation and rescales its O_t rows (output and
@@ -33,17 +39,18 @@
 namespace b2 {
 
 struct AttnPairCfg {
-  static constexpr int kThreads = 320;
+  static constexpr int kThreads = 352;
   static constexpr int kBoxBytes = 128 * 128;          // 128 rows x 64 bf16 columns
   static constexpr int kQBytes = kBoxBytes;            // one 128 x 64 query tile
   static constexpr int kKBytes = kBoxBytes;
-  static constexpr int kVStageBytes = 2 * kBoxBytes;   // V tile + block of ones
+  static constexpr int kVBytes = kBoxBytes;
   static constexpr int kPBytes = 2 * kBoxBytes;        // 128 rows x 128 keys bf16
-  static constexpr int kStages = 2;
+  static constexpr int kStages = 3;
   static constexpr int kOffQ = 0;                                   // [2]
   static constexpr int kOffK = kOffQ + 2 * kQBytes;                 // [kStages]
   static constexpr int kOffV = kOffK + kStages * kKBytes;           // [kStages]
-  static constexpr int kOffP = kOffV + kStages * kVStageBytes;      // [2 groups]
+  static constexpr int kOffOnes = kOffV + kStages * kVBytes;        // one 128 x 64 block of bf16 ones
+  static constexpr int kOffP = kOffOnes + kBoxBytes;                // [2 groups]
   static constexpr int kOffBar = kOffP + 2 * kPBytes;
   static constexpr int kSmemBytes = kOffBar + 256 + 1024;
   static constexpr int kTmemCols = 512;
@@ -77,15 +84,16 @@ __global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
   uint8_t* s_p = smem + Cfg::kOffP;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;   // [2]
-  uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;   // [2]
-  uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;   // [2 groups]
-  uint64_t* p_full = bars + 11;  // [2 groups]
-  uint64_t* o_full = bars + 13;  // [2 groups]
-  uint64_t* drain = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* k_full = bars + 1;    // [kStages]
+  uint64_t* k_empty = bars + 4;   // [kStages]
+  uint64_t* v_full = bars + 7;    // [kStages]
+  uint64_t* v_empty = bars + 10;  // [kStages]
+  uint64_t* s_full = bars + 13;   // [2 groups]
+  uint64_t* p_full = bars + 15;   // [2 groups]
+  uint64_t* o_full = bars + 17;   // [2 groups]
+  uint64_t* s_free = bars + 19;   // [2 groups]
+  uint64_t* drain = bars + 21;    // [2 issuers]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 23);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -110,16 +118,20 @@ __global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < Cfg::kStages; ++i) {
       mbar_init(&k_full[i], 1);
-      mbar_init(&k_empty[i], 1);
+      mbar_init(&k_empty[i], 2);
       mbar_init(&v_full[i], 1);
-      mbar_init(&v_empty[i], 1);
+      mbar_init(&v_empty[i], 2);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4);
       mbar_init(&o_full[i], 1);
+      mbar_init(&s_free[i], 4);
     }
-    mbar_init(drain, 1);
+    mbar_init(&drain[0], 1);
+    mbar_init(&drain[1], 1);
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -128,8 +140,8 @@ __global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
     tmem_relinquish();
   }
-  for (int st = 0; st < Cfg::kStages; ++st) {
-    uint4* ones = reinterpret_cast<uint4*>(s_v + st * Cfg::kVStageBytes + Cfg::kBoxBytes);
+  {
+    uint4* ones = reinterpret_cast<uint4*>(smem + Cfg::kOffOnes);
     for (int i = threadIdx.x; i < Cfg::kBoxBytes / 16; i += Cfg::kThreads)
       ones[i] = make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
   }
@@ -148,114 +160,139 @@ __global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
       mbar_arrive_expect_tx(q_full, 2 * Cfg::kQBytes);
       tma_load_2d(s_q, &tm_qkv, q_full, qc, q_row0);
       tma_load_2d(s_q + Cfg::kQBytes, &tm_qkv, q_full, qc, q_row0 + 128);
-      int issued_k = 0, issued_v = 0;
+      // K and V rings refill independently (polling both), so a K tile never waits for a V slot.
+      int k_next = 0, v_next = 0;
       bool ok = true;
-      for (int j = 0; j < n_total; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        const int krow = row_base + j * 128;
-        if (!mbar_wait(&k_empty[st], ph ^ 1u, abort_flag, kKernelAttention, 21)) {
+      PollTimeout poll;
+      poll.reset();
+      while (k_next < n_total || v_next < n_total) {
+        bool progress = false;
+        if (k_next < n_total &&
+            mbar_test_wait(&k_empty[k_next % Cfg::kStages], ((k_next / Cfg::kStages) & 1) ^ 1u)) {
+          const int st = k_next % Cfg::kStages;
+          mbar_arrive_expect_tx(&k_full[st], Cfg::kKBytes);
+          tma_load_2d(s_k + st * Cfg::kKBytes, &tm_qkv, &k_full[st], kc, row_base + k_next * 128);
+          ++k_next;
+          progress = true;
+        }
+        if (v_next < n_total &&
+            mbar_test_wait(&v_empty[v_next % Cfg::kStages], ((v_next / Cfg::kStages) & 1) ^ 1u)) {
+          const int st = v_next % Cfg::kStages;
+          mbar_arrive_expect_tx(&v_full[st], Cfg::kVBytes);
+          tma_load_2d(s_v + st * Cfg::kVBytes, &tm_qkv, &v_full[st], vc, row_base + v_next * 128);
+          ++v_next;
+          progress = true;
+        }
+        if (progress) {
+          poll.reset();
+        } else if (*abort_flag) {
+          ok = false;
+          break;
+        } else if (poll.expired()) {
+          record_status(kKernelAttention, 21, kReasonTimeout);
+          *abort_flag = 1;
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&k_full[st], Cfg::kKBytes);
-        tma_load_2d(s_k + st * Cfg::kKBytes, &tm_qkv, &k_full[st], kc, krow);
-        ++issued_k;
-        if (!mbar_wait(&v_empty[st], ph ^ 1u, abort_flag, kKernelAttention, 22)) {
-          ok = false;
-          break;
-        }
-        mbar_arrive_expect_tx(&v_full[st], Cfg::kBoxBytes);
-        tma_load_2d(s_v + st * Cfg::kVStageBytes, &tm_qkv, &v_full[st], vc, krow);
-        ++issued_v;
       }
       if (!ok) {
+        // Let copies in flight land: Q and the last (up to kStages) K and V tiles.
         const uint64_t t0 = global_timer_ns();
         auto drain_wait = [&](uint64_t* bar, uint32_t par) {
           while (!mbar_try_wait(bar, par) && global_timer_ns() - t0 < kWaitTimeoutNs) {
           }
         };
         drain_wait(q_full, 0);
-        for (int j = issued_k - 1; j >= 0 && j >= issued_k - 2; --j) drain_wait(&k_full[j & 1], (j >> 1) & 1);
-        for (int j = issued_v - 1; j >= 0 && j >= issued_v - 2; --j) drain_wait(&v_full[j & 1], (j >> 1) & 1);
+        for (int j = k_next - 1; j >= 0 && j >= k_next - Cfg::kStages; --j)
+          drain_wait(&k_full[j % Cfg::kStages], (j / Cfg::kStages) & 1);
+        for (int j = v_next - 1; j >= 0 && j >= v_next - Cfg::kStages; --j)
+          drain_wait(&v_full[j % Cfg::kStages], (j / Cfg::kStages) & 1);
       }
     }
-  } else if (warp == 1) {
-    // ---------------- UMMA issuer ----------------
+  } else if (warp == 1 || warp == 2) {
+    // ---------------- UMMA issuers (one per group) ----------------
+    const int t = warp - 1;
     if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc_bf16_f32(128, 128, 0, 0);
       constexpr uint32_t idesc_o = make_idesc_bf16_f32(128, Cfg::kON, 0, 1);
-      const uint32_t q_addr = smem_u32(s_q);
-      auto issue_s = [&](int t, int j) {
-        const uint32_t k_addr = smem_u32(s_k + (j & 1) * Cfg::kKBytes);
-        const uint32_t a0 = q_addr + t * Cfg::kQBytes;
-        const uint32_t d = tmem_base + Cfg::kSCol + t * 128;
+      const uint32_t q_addr = smem_u32(s_q) + t * Cfg::kQBytes;
+      const uint32_t d_s = tmem_base + Cfg::kSCol + t * 128;
+      const uint32_t d_o = tmem_base + Cfg::kOCol + t * 128;
+      const int n = n_kv[t];
+      auto issue_s = [&](int j) {
+        const uint32_t k_addr = smem_u32(s_k + (j % Cfg::kStages) * Cfg::kKBytes);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk)
-          umma_bf16_ss(d, make_sdesc_sw128(a0 + kk * 32, 16, 1024), make_sdesc_sw128(k_addr + kk * 32, 16, 1024),
-                       idesc_s, kk > 0 ? 1u : 0u);
+          umma_bf16_ss(d_s, make_sdesc_sw128(q_addr + kk * 32, 16, 1024),
+                       make_sdesc_sw128(k_addr + kk * 32, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
         umma_commit(&s_full[t]);
+        umma_commit(&k_empty[j % Cfg::kStages]);
       };
-      auto issue_o = [&](int t, int j) {
+      auto issue_o = [&](int j) {
         const uint32_t p_addr = smem_u32(s_p + t * Cfg::kPBytes);
-        const uint32_t v_addr = smem_u32(s_v + (j & 1) * Cfg::kVStageBytes);
-        const uint32_t d = tmem_base + Cfg::kOCol + t * 128;
+        const int vst = j % Cfg::kStages;
+        const uint32_t v_addr = smem_u32(s_v + vst * Cfg::kVBytes);
+        const uint32_t ones_lbo = static_cast<uint32_t>(Cfg::kOffOnes - Cfg::kOffV - vst * Cfg::kVBytes);
 #pragma unroll
         for (int kk = 0; kk < 128 / 16; ++kk)
-          umma_bf16_ss(d, make_sdesc_sw128(p_addr + (kk >> 2) * Cfg::kBoxBytes + (kk & 3) * 32, 16, 1024),
-                       make_sdesc_sw128(v_addr + kk * 2048, Cfg::kBoxBytes, 1024), idesc_o,
-                       (j > 0 || kk > 0) ? 1u : 0u);
+          umma_bf16_ss(d_o, make_sdesc_sw128(p_addr + (kk >> 2) * Cfg::kBoxBytes + (kk & 3) * 32, 16, 1024),
+                       make_sdesc_sw128(v_addr + kk * 2048, ones_lbo, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&o_full[t]);
+        umma_commit(&v_empty[vst]);
       };
-      bool ok = mbar_wait(q_full, 0, abort_flag, kKernelAttention, 23) &&
-                mbar_wait(&k_full[0], 0, abort_flag, kKernelAttention, 24);
-      if (ok) {
+      bool ok = n == 0 || mbar_wait(q_full, 0, abort_flag, kKernelAttention, 23);
+      for (int j = 0; j < n && ok; ++j) {
+        // S_t(j): K_j loaded and (j > 0) S_t(j-1) taken by the softmax group.
+        if (!mbar_wait(&k_full[j % Cfg::kStages], (j / Cfg::kStages) & 1, abort_flag, kKernelAttention, 24) ||
+            (j > 0 && !mbar_wait(&s_free[t], (j - 1) & 1, abort_flag, kKernelAttention, 25))) {
+          ok = false;
+          break;
+        }
         tc_fence_after_sync();
-        for (int t = 0; t < 2; ++t)
-          if (n_kv[t] > 0) issue_s(t, 0);
-        umma_commit(&k_empty[0]);
-      }
-      for (int j = 0; j < n_total && ok; ++j) {
-        bool k_next_ready = false, v_ready = false;
-        for (int t = 0; t < 2 && ok; ++t) {
-          if (j >= n_kv[t]) continue;
-          // Group t is done with S_t(j) and O_t(j-1), and P_t(j) is in shared memory.
-          if (!mbar_wait(&p_full[t], j & 1, abort_flag, kKernelAttention, 25)) {
+        issue_s(j);
+        // O_t += P_t(j-1) V_{j-1} once published (issued after S_t(j) so the scores come first).
+        if (j > 0) {
+          if (!mbar_wait(&p_full[t], (j - 1) & 1, abort_flag, kKernelAttention, 26) ||
+              !mbar_wait(&v_full[(j - 1) % Cfg::kStages], ((j - 1) / Cfg::kStages) & 1, abort_flag,
+                         kKernelAttention, 27)) {
             ok = false;
             break;
           }
-          if (j + 1 < n_kv[t]) {
-            if (!k_next_ready) {
-              if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, kKernelAttention, 26)) {
-                ok = false;
-                break;
-              }
-              k_next_ready = true;
-            }
-            tc_fence_after_sync();
-            issue_s(t, j + 1);
-            if (t == 1 || n_kv[1] <= j + 1) umma_commit(&k_empty[(j + 1) & 1]);  // last reader of K_{j+1}
-          }
-          if (!v_ready) {
-            if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1, abort_flag, kKernelAttention, 27)) {
-              ok = false;
-              break;
-            }
-            v_ready = true;
-          }
           tc_fence_after_sync();
-          issue_o(t, j);
-          if (t == 1 || n_kv[1] <= j) umma_commit(&v_empty[j & 1]);  // last reader of V_j
+          issue_o(j - 1);
         }
       }
-      umma_commit(drain);
+      if (ok && n > 0) {
+        if (!mbar_wait(&p_full[t], (n - 1) & 1, abort_flag, kKernelAttention, 26) ||
+            !mbar_wait(&v_full[(n - 1) % Cfg::kStages], ((n - 1) / Cfg::kStages) & 1, abort_flag, kKernelAttention,
+                       27)) {
+          ok = false;
+        } else {
+          tc_fence_after_sync();
+          issue_o(n - 1);
+        }
+      }
+      // K/V tiles this group does not use: release each slot for the producer once its previous
+      // use is over (a plain arrive here would otherwise count toward the previous phase).
+      for (int j = n; j < n_total && ok; ++j) {
+        const int st = j % Cfg::kStages;
+        const uint32_t prev = ((j / Cfg::kStages) & 1) ^ 1u;
+        if (!mbar_wait(&k_empty[st], prev, abort_flag, kKernelAttention, 31) ||
+            !mbar_wait(&v_empty[st], prev, abort_flag, kKernelAttention, 32)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive(&k_empty[st]);
+        mbar_arrive(&v_empty[st]);
+      }
+      umma_commit(&drain[t]);
       const uint64_t t0 = global_timer_ns();
-      while (!mbar_try_wait(drain, 0) && global_timer_ns() - t0 < kWaitTimeoutNs) {
+      while (!mbar_try_wait(&drain[t], 0) && global_timer_ns() - t0 < kWaitTimeoutNs) {
       }
     }
   } else {
     // ---------------- softmax groups ----------------
-    const int grp = (warp - 2) >> 2;
+    const int grp = (warp - 3) >> 2;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     const int qt = 2 * pair + grp;
@@ -272,59 +309,99 @@ __global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
     float m_ref = 0.f;  // reference maximum (raw score units) used in exp2(c * (s - m_ref))
     bool alive = true;
 
+    // Ping-pong of the exponential phase between the groups: group g runs its exp2 loop only
+    // after the other group finished its previous one (named barrier 1 + g completes when the 128
+    // threads of group g sync and the 128 of the other group arrive), so each SM sub-partition's
+    // exponential unit (16/clk/SM) serves one group while the other loads and reduces its next
+    // score tile. Both groups run n_total rounds (idle rounds only pass the barriers) so the
+    // arrive/sync counts match; group 1 pre-arrives once and skips its last arrive.
+    if (grp == 1) named_barrier_arrive(1, 256);
+
 #pragma unroll 1
-    for (int j = 0; j < n; ++j) {
-      softmax_wait(&s_full[grp], j & 1, 28, alive, abort_flag);
-      tc_fence_after_sync();
-      float v[128];
-      tmem_load_128cols(t_s, v);
-      if (j == n - 1) {
-        const int n_valid = limit - j * 128;  // keys [0, n_valid) of the last tile are visible
-#pragma unroll
-        for (int k = 0; k < 128; ++k) v[k] = (k < n_valid) ? v[k] : -INFINITY;
-      }
-      const float rmax = fmaxf(fmaxf(max32(v), max32(v + 32)), fmaxf(max32(v + 64), max32(v + 96)));
+    for (int j = 0; j < n_total; ++j) {
+      const bool work = j < n;
+      const bool last = j == n - 1;
+      const int n_valid = limit - j * 128;  // keys [0, n_valid) of the last tile are visible
       float alpha = 1.f;  // < 1 when this row's reference maximum moves (rare after the first tile)
-      if (j == 0) {
-        m_ref = rmax == -INFINITY ? 0.f : rmax;
-      } else if ((rmax - m_ref) * c > kRescaleThreshold) {
-        alpha = fast_exp2((m_ref - rmax) * c);
-        m_ref = rmax;
-      }
-      const float neg_mc = -m_ref * c;
-      // probabilities -> P_t: row r, keys 8q..8q+7 = 16-byte chunk (q % 8) of atom q / 8
-#pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        uint32_t w[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float e0 = fast_exp2(fmaf(v[8 * q + 2 * k], c, neg_mc));
-          const float e1 = fast_exp2(fmaf(v[8 * q + 2 * k + 1], c, neg_mc));
-          w[k] = pack_bf16x2(e0, e1);
-        }
-        *reinterpret_cast<uint4*>(prow + (q >> 3) * Cfg::kBoxBytes + (((q & 7) ^ (r & 7)) << 4)) =
-            make_uint4(w[0], w[1], w[2], w[3]);
-      }
-      if (__any_sync(0xffffffffu, alpha < 1.f)) {
-        // Rescale the accumulated output and row sums (P_t(0..j-1) V) of the warp's rows to their
-        // new reference maxima (alpha = 1 for rows whose maximum did not move) once the
-        // accumulation of tile j-1 has landed, before P_t(j) V is accumulated. Warp-uniform: the
-        // TMEM loads and stores are warp-collective.
-        softmax_wait(&o_full[grp], (j - 1) & 1, 29, alive, abort_flag);
+      if (work) {
+        // Row maximum first (scores are read again after the handoff, so none are held across it).
+        softmax_wait(&s_full[grp], j & 1, 28, alive, abort_flag);
         tc_fence_after_sync();
-#pragma unroll 1
-        for (int cc = 0; cc < 3; ++cc) {
-          float o[32];
-          tmem_load_32cols(t_o + cc * 32, o);
+        float rmax;
+        {
+          float v[128];
+          tmem_load_128cols(t_s, v);
+          if (last) {
 #pragma unroll
-          for (int k = 0; k < 32; ++k) o[k] *= alpha;
-          tmem_store_32cols(t_o + cc * 32, o);
+            for (int k = 0; k < 128; ++k) v[k] = (k < n_valid) ? v[k] : -INFINITY;
+          }
+          rmax = fmaxf(fmaxf(max32(v), max32(v + 32)), fmaxf(max32(v + 64), max32(v + 96)));
+        }
+        if (j == 0) {
+          m_ref = rmax == -INFINITY ? 0.f : rmax;
+        } else if ((rmax - m_ref) * c > kRescaleThreshold) {
+          alpha = fast_exp2((m_ref - rmax) * c);
+          m_ref = rmax;
+        }
+        // P_t(j-1) V must have been accumulated before P_t is overwritten (and before a rescale).
+        if (j > 0) {
+          softmax_wait(&o_full[grp], (j - 1) & 1, 29, alive, abort_flag);
+          tc_fence_after_sync();
         }
       }
-      fence_proxy_async_smem();
-      tc_fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[grp]);
+      if (grp == 0)
+        named_barrier_sync(1, 256);
+      else
+        named_barrier_sync(2, 256);
+      if (work) {
+        float v[128];
+        tmem_load_128cols(t_s, v);
+        tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[grp]);  // S_t may now receive tile j + 1
+        if (last) {
+#pragma unroll
+          for (int k = 0; k < 128; ++k) v[k] = (k < n_valid) ? v[k] : -INFINITY;
+        }
+        const float neg_mc = -m_ref * c;
+        // probabilities -> P_t: row r, keys 8q..8q+7 = 16-byte chunk (q % 8) of atom q / 8
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          uint32_t w[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float e0 = fast_exp2(fmaf(v[8 * q + 2 * k], c, neg_mc));
+            const float e1 = fast_exp2(fmaf(v[8 * q + 2 * k + 1], c, neg_mc));
+            w[k] = pack_bf16x2(e0, e1);
+          }
+          *reinterpret_cast<uint4*>(prow + (q >> 3) * Cfg::kBoxBytes + (((q & 7) ^ (r & 7)) << 4)) =
+              make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      if (grp == 0)
+        named_barrier_arrive(2, 256);
+      else if (j < n_total - 1)
+        named_barrier_arrive(1, 256);
+      if (work) {
+        if (__any_sync(0xffffffffu, alpha < 1.f)) {
+          // Rescale the accumulated output and row sums (P_t(0..j-1) V) of the warp's rows to their
+          // new reference maxima (alpha = 1 for rows whose maximum did not move); the accumulation
+          // of tile j-1 has landed (waited above) and P_t(j) V is not issued before p_full_t.
+          // Warp-uniform: the TMEM loads and stores are warp-collective.
+#pragma unroll 1
+          for (int cc = 0; cc < 3; ++cc) {
+            float o[32];
+            tmem_load_32cols(t_o + cc * 32, o);
+#pragma unroll
+            for (int k = 0; k < 32; ++k) o[k] *= alpha;
+            tmem_store_32cols(t_o + cc * 32, o);
+          }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[grp]);
+      }
     }
 
     if (n > 0) {

@@ -36,6 +36,29 @@ __device__ __forceinline__ void record_status(uint32_t kernel_id, uint32_t site,
   atomicCAS(&g_device_status, 0u, (kernel_id << 16) | (site << 8) | reason);
 }
 
+// Bounded polling loops (several barriers serviced by one thread) count idle spins and read the
+// SM-local clock only every kPollCheckSpins idle spins; kPollTimeoutCycles ~ 4 s at 2 GHz.
+constexpr uint32_t kPollCheckSpins = 256;
+constexpr long long kPollTimeoutCycles = 8000000000ll;
+
+struct PollTimeout {
+  long long start;
+  uint32_t idle;
+  __device__ __forceinline__ void reset() {
+    idle = 0;
+    start = clock64();
+  }
+  // Call on an iteration that made no progress; true when the loop has been idle too long.
+  // Sleeps briefly so the polling warp does not take issue slots from the compute warps that
+  // share its SM sub-partition.
+  __device__ __forceinline__ bool expired() {
+    __nanosleep(32);
+    if (++idle < kPollCheckSpins) return false;
+    idle = 0;
+    return clock64() - start > kPollTimeoutCycles;
+  }
+};
+
 // Limit for one mbarrier wait. Legitimate waits in these kernels are microseconds long
 // (the longest is an epilogue waiting for one full K loop); 4 s means the pipeline is stuck.
 constexpr uint64_t kWaitTimeoutNs = 4000000000ull;
@@ -88,6 +111,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// Non-blocking probe of the same condition (mbarrier.test_wait never suspends the thread, unlike
+// try_wait, which may sleep for a hardware time slice when the phase is incomplete). For loops that
+// poll several barriers and must react to whichever completes first.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 // Waits until the phase of `bar` with parity `parity` has completed. Returns false (after
 // recording a status word and raising *abort) when the wait exceeds kWaitTimeoutNs, and false
 // without recording when another role of the CTA already raised *abort.
@@ -105,6 +143,24 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
         *abort = 1;
         return false;
       }
+    }
+  }
+}
+
+// Same contract as mbar_wait, but spins on the non-suspending test_wait: lower wake-up latency for
+// waits on the critical path of a pipeline (the thread is not parked by the hardware).
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                               uint32_t kernel_id, uint32_t site) {
+  if (mbar_test_wait(bar, parity)) return true;
+  PollTimeout poll;
+  poll.reset();
+  while (true) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if (*abort) return false;
+    if (poll.expired()) {
+      record_status(kernel_id, site, kReasonTimeout);
+      *abort = 1;
+      return false;
     }
   }
 }
@@ -335,6 +391,20 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   float r;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
   return r;
+}
+
+// a = a * m + d and b = b * m + d with one packed fp32x2 FMA (sm_100).
+__device__ __forceinline__ void fma2_inplace(float& a, float& b, uint64_t m2, uint64_t d2) {
+  uint64_t x;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(a), "f"(b));
+  asm("fma.rn.f32x2 %0, %0, %1, %2;" : "+l"(x) : "l"(m2), "l"(d2));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(x));
+}
+
+__device__ __forceinline__ uint64_t splat2(float v) {
+  uint64_t x;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(x) : "f"(v));
+  return x;
 }
 
 __device__ __forceinline__ float fast_exp2(float x) {
