@@ -103,6 +103,28 @@ class TensorParallelTransformer:
         self.final_b = full["final_norm.bias"].contiguous()
         self.eps = 1e-5
         self._mask_lengths = MaskLengths()
+        self._launch_log: Optional[list] = None
+
+    def record_launches(self, enabled: bool) -> None:
+        """When enabled, every kernel launch and all-reduce is bracketed by CUDA events."""
+        self._launch_log = [] if enabled else None
+
+    def take_launch_log(self) -> list:
+        log = self._launch_log or []
+        if self._launch_log is not None:
+            self._launch_log = []
+        return log
+
+    def _timed(self, kind: str, fn, *args, **kwargs) -> None:
+        if self._launch_log is None:
+            fn(*args, **kwargs)
+            return
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record()
+        fn(*args, **kwargs)
+        end.record()
+        self._launch_log.append((kind, start, end))
 
     def _all_reduce(self, t: torch.Tensor) -> None:
         import torch.distributed as dist
@@ -133,21 +155,24 @@ class TensorParallelTransformer:
         out = torch.empty(batch, seq_len, d, device=dev, dtype=torch.bfloat16)
         x2 = x.contiguous().view(tokens, d)
         s0 = self.shards[0]
-        _capi.layernorm(x2, s0["ln1_w"], s0["ln1_b"], self.eps, ln, resid_out=resid)
+        t = self._timed
+        t("layernorm", _capi.layernorm, x2, s0["ln1_w"], s0["ln1_b"], self.eps, ln, resid_out=resid)
         for i, s in enumerate(self.shards):
-            _capi.linear(ln, s["w_qkv"], s["b_qkv"], _capi.EPI_BIAS, qkv)
-            _capi.attention(qkv, batch, seq_len, h_loc, hd, 0, d_loc, 2 * d_loc, kv_len, cfg.causal, hd**-0.5, ctx)
-            _capi.linear(ctx, s["w_o"], None, _capi.EPI_STORE_F32, part)
-            self._all_reduce(part)
-            _capi.add_layernorm(resid, part, s["b_o"], s["ln2_w"], s["ln2_b"], self.eps, ln, row_mask, 0)
-            _capi.linear(ln, s["w_1"], s["b_1"], _capi.EPI_BIAS_GELU, hidden)
-            _capi.linear(hidden, s["w_2"], None, _capi.EPI_STORE_F32, part)
-            self._all_reduce(part)
+            t("gemm_qkv", _capi.linear, ln, s["w_qkv"], s["b_qkv"], _capi.EPI_BIAS, qkv)
+            t("attention", _capi.attention, qkv, batch, seq_len, h_loc, hd, 0, d_loc, 2 * d_loc, kv_len, cfg.causal,
+              hd**-0.5, ctx)
+            t("gemm_out", _capi.linear, ctx, s["w_o"], None, _capi.EPI_STORE_F32, part)
+            t("allreduce", self._all_reduce, part)
+            t("layernorm", _capi.add_layernorm, resid, part, s["b_o"], s["ln2_w"], s["ln2_b"], self.eps, ln, row_mask,
+              0)
+            t("gemm_ffn_in", _capi.linear, ln, s["w_1"], s["b_1"], _capi.EPI_BIAS_GELU, hidden)
+            t("gemm_ffn_out", _capi.linear, hidden, s["w_2"], None, _capi.EPI_STORE_F32, part)
+            t("allreduce", self._all_reduce, part)
             last = i == len(self.shards) - 1
             g, b = (self.final_w, self.final_b) if last else (self.shards[i + 1]["ln1_w"], self.shards[i + 1]["ln1_b"])
             flags = _capi.ADD_LN_ZERO_ROWS | (_capi.ADD_LN_ZERO_Y if last else 0)
-            _capi.add_layernorm(resid, part, s["b_2"], g, b, self.eps, out.view(tokens, d) if last else ln, row_mask,
-                                flags)
+            t("layernorm", _capi.add_layernorm, resid, part, s["b_2"], g, b, self.eps,
+              out.view(tokens, d) if last else ln, row_mask, flags)
         return out
 
     __call__ = forward
