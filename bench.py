@@ -355,10 +355,13 @@ def main() -> None:
         d2h = y_host.numel() * y_host.element_size()
 
         # ---------------- per-kernel device times (roofline of the dominant kernel)
+        # Each eager forward is queued behind a ~20 ms GPU sleep, so the host enqueues every launch
+        # before the GPU reaches it and the per-launch events time the kernels, not launch overhead.
         model.record_launches(True)
         reps = 3
         for _ in range(reps):
             flush.fill_(1.0)
+            torch.cuda._sleep(40_000_000)
             model(x, use_mask)
         torch.cuda.synchronize()
         log = model.take_launch_log()

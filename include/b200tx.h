@@ -42,6 +42,10 @@ extern "C" {
 #define B2_EPI_RESIDUAL_ZERO 3  /* out f32 (in place) = mask ? out + acc + bias : 0      */
 #define B2_EPI_STORE_F32 4      /* out f32 = acc (+ bias if non-null)                     */
 
+/* b2_linear_fwd tile_n flag: the 2-SM variant (a CTA pair computes 256-row tiles with
+ * tcgen05.mma.cta_group::2), combined with an N tile of 192 or 256. */
+#define B2_TILE_PAIR 0x10000
+
 /* ABI revision of this header (1). */
 int b2_abi_version(void);
 
@@ -86,7 +90,8 @@ int b2_add_layernorm_fwd(float* resid, const float* delta, const void* bias, con
  *   a    [m, k] bf16;  w [n, k] bf16 (nn.Linear weight layout);  bias [n] bf16 or NULL
  *   out  [m, ldo] bf16 (B2_EPI_BIAS, B2_EPI_BIAS_GELU) or fp32 (others)
  *   row_mask [m] uint8 or NULL (residual epilogues only)
- *   tile_n 0 = choose, or 128 / 192 / 256 (192 and 256 need n to be a multiple)
+ *   tile_n 0 = choose; 128 / 192 / 256 = one CTA per 128 x tile_n tile; B2_TILE_PAIR | 192 / 256 =
+ *          a CTA pair per 256 x tile_n tile (192 and 256 need n to be a multiple)
  * Requires n % 32 == 0, k % 8 == 0, ldo % 8 == 0, 16-byte aligned pointers, an sm_100 device.
  */
 int b2_linear_fwd(const void* a, const void* w, const void* bias, int64_t m, int64_t n, int64_t k, int epilogue,

@@ -123,6 +123,41 @@ def test_gemm_store_f32_and_tile_choice_agree(m, n, k):
             assert torch.equal(out128, other), tile
 
 
+PAIR = 0x10000  # B2_TILE_PAIR
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 256, 64), (4096, 2304, 768), (1000, 3072, 768), (300, 768, 3072),
+                                   (4096, 768, 768), (32768, 1024, 1024)])
+@pytest.mark.parametrize("epi", ["bias", "gelu", "residual_zero", "f32"])
+def test_gemm_pair_tiles_match_fp32(m, n, k, epi):
+    """The 2-SM (CTA pair, 256-row tile) variant against fp32, every epilogue, N tiles 256 and 192."""
+    a, w, bias, ref = _gemm_inputs(m, n, k, 7)
+    for bn in (256, 192):
+        if n % bn:
+            continue
+        if epi in ("bias", "gelu"):
+            out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+            code = _capi.EPI_BIAS if epi == "bias" else _capi.EPI_BIAS_GELU
+            _capi.linear(a, w, bias, code, out, tile_n=PAIR | bn)
+            expect = ref if epi == "bias" else F.gelu(ref.bfloat16().float(), approximate="none")
+            torch.testing.assert_close(out.float(), expect, atol=2e-2, rtol=1e-2)
+        elif epi == "f32":
+            out = torch.empty(m, n, device="cuda")
+            _capi.linear(a, w, None, _capi.EPI_STORE_F32, out, tile_n=PAIR | bn)
+            one = torch.empty(m, n, device="cuda")
+            _capi.linear(a, w, None, _capi.EPI_STORE_F32, one, tile_n=128)
+            torch.testing.assert_close(out, one, atol=1e-5, rtol=1e-6)
+        else:
+            g = _gen(8)
+            resid0 = torch.randn(m, n, device="cuda", generator=g)
+            mask = (torch.rand(m, device="cuda", generator=g) > 0.25).to(torch.uint8)
+            resid = resid0.clone()
+            _capi.linear(a, w, bias, _capi.EPI_RESIDUAL_ZERO, resid, row_mask=mask, tile_n=PAIR | bn)
+            keep = mask.bool()[:, None]
+            torch.testing.assert_close(resid, torch.where(keep, resid0 + ref, torch.zeros_like(resid0)),
+                                       atol=2e-3, rtol=1e-4)
+
+
 def test_gemm_is_row_invariant():
     """Each output row depends only on its own input row: a sub-batch gives bit-identical rows."""
     a, w, bias, _ = _gemm_inputs(1536, 1024, 1024, 6)

@@ -192,6 +192,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait_previous_grid();
+  pdl_allow_next_grid();
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -425,8 +427,7 @@ static cudaError_t launch_attention_t(const CUtensorMap& tm, const AttnParams& p
   });
   if (attr_err != cudaSuccess) return attr_err;
   dim3 grid(p.B * p.H, p.n_q_tiles);
-  attention_tc_kernel<HD><<<grid, kAttnThreads, Cfg::kSmemBytes, stream>>>(tm, p);
-  return cudaGetLastError();
+  return launch_pdl(attention_tc_kernel<HD>, grid, dim3(kAttnThreads), Cfg::kSmemBytes, stream, tm, p);
 }
 
 static cudaError_t launch_attention_pair(const CUtensorMap& tm, const AttnParams& p, cudaStream_t stream);

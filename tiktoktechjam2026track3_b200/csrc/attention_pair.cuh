@@ -150,6 +150,8 @@ __global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait_previous_grid();
+  pdl_allow_next_grid();
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -442,8 +444,7 @@ static cudaError_t launch_attention_pair(const CUtensorMap& tm, const AttnParams
   });
   if (attr_err != cudaSuccess) return attr_err;
   dim3 grid(p.B * p.H, (p.n_q_tiles + 1) / 2);
-  attention_pair_kernel<<<grid, AttnPairCfg::kThreads, AttnPairCfg::kSmemBytes, stream>>>(tm, p);
-  return cudaGetLastError();
+  return launch_pdl(attention_pair_kernel, grid, dim3(AttnPairCfg::kThreads), AttnPairCfg::kSmemBytes, stream, tm, p);
 }
 
 }  // namespace b2

@@ -137,10 +137,15 @@ B2_API int b2_linear_fwd(const void* a, const void* w, const void* bias, int64_t
   if (n % 32 != 0) return fail(2, "b2_linear_fwd: n=%lld must be a multiple of 32", (long long)n);
   if (k % 8 != 0) return fail(2, "b2_linear_fwd: k=%lld must be a multiple of 8", (long long)k);
   if (ldo < n || ldo % 8 != 0) return fail(2, "b2_linear_fwd: ldo=%lld must be >= n and a multiple of 8", (long long)ldo);
-  if (tile_n != 0 && tile_n != 128 && tile_n != 192 && tile_n != 256)
-    return fail(1, "b2_linear_fwd: tile_n must be 0, 128, 192 or 256");
-  if ((tile_n == 256 || tile_n == 192) && n % tile_n != 0)
-    return fail(2, "b2_linear_fwd: tile_n=%d needs n %% %d == 0", tile_n, tile_n);
+  {
+    const int bn = tile_n & 0xFFFF;
+    const bool pair = (tile_n & kTilePair) != 0;
+    if ((tile_n & ~(kTilePair | 0xFFFF)) != 0 || (tile_n != 0 && bn != 128 && bn != 192 && bn != 256) ||
+        (pair && bn == 128))
+      return fail(1, "b2_linear_fwd: tile_n must be 0, 128, 192, 256, or B2_TILE_PAIR | 192 / 256");
+    if ((bn == 256 || bn == 192) && n % bn != 0)
+      return fail(2, "b2_linear_fwd: an N tile of %d needs n %% %d == 0", bn, bn);
+  }
   if (!aligned16(a) || !aligned16(w) || !aligned16(out) || (bias && !aligned16(bias)))
     return fail(2, "b2_linear_fwd: pointers must be 16-byte aligned");
   if (m > 0x7fffff00LL || n > 0x7fffff00LL) return fail(2, "b2_linear_fwd: dimension exceeds 2^31");

@@ -182,6 +182,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait_previous_grid();
+  pdl_allow_next_grid();
 
   const int num_tiles = p.m_blocks * p.n_blocks;
 
@@ -303,6 +305,191 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 // ---------------------------------------------------------------------------------------------
+// 2-SM variant: a cluster of 2 CTAs computes a 256 x BN tile with tcgen05.mma.cta_group::2. CTA
+// p of the pair loads A rows [128p, 128p + 128) and W rows [BN/2 p, BN/2 (p+1)) of the tile
+// (32 KB per 64-deep k-block for BN = 256, against 48 KB per CTA for a 128 x 256 one-CTA tile), so
+// every byte fetched from L2 feeds 1.5x more MMA work, and the 32 KB stages allow a 6-deep ring.
+// The leader (rank 0) issues the MMAs; both CTAs' TMA loads count on the leader's full barrier;
+// the leader's commits reach both CTAs' empty / accumulator barriers; each CTA's epilogue drains
+// its own 128 accumulator rows and reports to the leader's acc_empty barrier.
+// ---------------------------------------------------------------------------------------------
+template <int BN>
+struct Gemm2Cfg {
+  static constexpr int kStages = 6;
+  static constexpr int kABytes = 128 * kGemmBK * 2;             // this CTA's 128 rows of A
+  static constexpr int kBBytes = (BN / 2) * kGemmBK * 2;        // this CTA's BN/2 rows of W
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kAccStride = 256;
+  static constexpr int kTmemCols = 512;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+};
+
+template <int BN, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                    const GemmParams p) {
+  using Cfg = Gemm2Cfg<BN>;
+  constexpr int kStages = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* s_a = smem;
+  uint8_t* s_b = smem + kStages * Cfg::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_b + kStages * Cfg::kBBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* acc_full = empty + kStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = static_cast<int>(cluster_id_x());
+  const int n_pairs = static_cast<int>(cluster_count_x());
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 2 * kGemmEpilogueThreads);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_a);
+    tma_prefetch_desc(&tm_b);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before_sync();
+  cluster_sync_all();  // both CTAs' barriers exist before any remote arrive / transaction
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_wait_previous_grid();
+  pdl_allow_next_grid();
+
+  const int m_tiles = (p.M + 255) / 256;
+  const int num_tiles = m_tiles * p.n_blocks;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += n_pairs) {
+        const int m_blk = tile / p.n_blocks;
+        const int n_blk = tile % p.n_blocks;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, kKernelGemm, 11)) {
+            ok = false;
+            break;
+          }
+          const uint32_t bar = cluster_map_to_rank(&full[s], 0);
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * Cfg::kStageBytes);
+          tma_load_2d_pair(s_a + s * Cfg::kABytes, &tm_a, bar, kb * kGemmBK, m_blk * 256 + rank * 128);
+          tma_load_2d_pair(s_b + s * Cfg::kBBytes, &tm_b, bar, kb * kGemmBK, n_blk * BN + rank * (BN / 2));
+          if (++s == kStages) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = make_idesc_bf16_f32(256, BN, 0, 0);
+      int s = 0;
+      uint32_t ph = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += n_pairs, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_ph = (local >> 1) & 1;
+        if (!mbar_wait_cluster(&acc_empty[acc], acc_ph ^ 1u, abort_flag, kKernelGemm, 12)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after_sync();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Cfg::kAccStride);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full[s], ph, abort_flag, kKernelGemm, 13)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after_sync();
+          const uint32_t a_addr = smem_u32(s_a + s * Cfg::kABytes);
+          const uint32_t b_addr = smem_u32(s_b + s * Cfg::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kGemmBK / 16; ++k)
+            umma_bf16_ss_pair(d_tmem, make_sdesc_sw128(a_addr + k * 32, 16, 1024),
+                              make_sdesc_sw128(b_addr + k * 32, 16, 1024), idesc, (kb | k) != 0 ? 1u : 0u);
+          umma_commit_pair(&empty[s], 0x3);
+          if (++s == kStages) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(&acc_full[acc], 0x3);
+      }
+      umma_commit(drain);
+      mbar_drain_wait(drain, 0);
+    }
+  } else {
+    // Two warps per TMEM lane quadrant; each covers one half of the tile's columns.
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row_in_tile = static_cast<int>(rank) * 128 + quad * 32 + lane;
+    const uint32_t acc_empty_leader0 = cluster_map_to_rank(&acc_empty[0], 0);
+    const uint32_t acc_empty_leader1 = cluster_map_to_rank(&acc_empty[1], 0);
+    int local = 0;
+    for (int tile = pair; tile < num_tiles; tile += n_pairs, ++local) {
+      const int m_blk = tile / p.n_blocks;
+      const int n_blk = tile % p.n_blocks;
+      const int acc = local & 1;
+      const uint32_t acc_ph = (local >> 1) & 1;
+      if (!mbar_wait(&acc_full[acc], acc_ph, abort_flag, kKernelGemm, 14)) break;
+      tc_fence_after_sync();
+      const int row = m_blk * 256 + row_in_tile;
+      const uint32_t t_row =
+          tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * Cfg::kAccStride);
+#pragma unroll 1
+      for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+        const int col0 = n_blk * BN + c * 32;
+        if (col0 >= p.N) break;  // warp-uniform
+        float v[32];
+        tmem_load_32cols(t_row + c * 32, v);
+        if (row < p.M) gemm_epilogue_chunk<EPI>(p, row, col0, v);
+      }
+      tc_fence_before_sync();
+      mbar_arrive_cluster(acc ? acc_empty_leader1 : acc_empty_leader0);
+    }
+  }
+
+  if (*abort_flag && threadIdx.x == 0) {
+    // A wait gave up: give TMA loads still in flight into this CTA's shared memory time to land.
+    const uint64_t t0 = global_timer_ns();
+    while (global_timer_ns() - t0 < 200000ull) {
+    }
+  }
+  __syncthreads();
+  cluster_sync_all();  // no CTA leaves while its pair may still arrive on its barriers
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------------------------
 cudaError_t make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
@@ -322,8 +509,42 @@ static cudaError_t launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, c
                                     Cfg::kSmemBytes);
   });
   if (attr_err != cudaSuccess) return attr_err;
-  gemm_tc_kernel<BN, EPI><<<grid, kGemmThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
-  return cudaGetLastError();
+  return launch_pdl(gemm_tc_kernel<BN, EPI>, dim3(grid), dim3(kGemmThreads), Cfg::kSmemBytes, stream, ta, tb, p);
+}
+
+template <int BN, int EPI>
+static cudaError_t launch_gemm2_t(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid,
+                                  cudaStream_t stream) {
+  using Cfg = Gemm2Cfg<BN>;
+  static std::once_flag once[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaError_t attr_err = cudaSuccess;
+  std::call_once(once[dev & 63], [&] {
+    attr_err = cudaFuncSetAttribute(gemm_tc2_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    Cfg::kSmemBytes);
+  });
+  if (attr_err != cudaSuccess) return attr_err;
+  return launch_pdl(gemm_tc2_kernel<BN, EPI>, dim3(grid), dim3(kGemmThreads), Cfg::kSmemBytes, stream, ta, tb, p);
+}
+
+template <int BN>
+static cudaError_t dispatch_epi2(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid,
+                                 cudaStream_t stream) {
+  switch (epi) {
+    case kEpiBias:
+      return launch_gemm2_t<BN, kEpiBias>(ta, tb, p, grid, stream);
+    case kEpiBiasGelu:
+      return launch_gemm2_t<BN, kEpiBiasGelu>(ta, tb, p, grid, stream);
+    case kEpiResidual:
+      return launch_gemm2_t<BN, kEpiResidual>(ta, tb, p, grid, stream);
+    case kEpiResidualZero:
+      return launch_gemm2_t<BN, kEpiResidualZero>(ta, tb, p, grid, stream);
+    case kEpiStoreF32:
+      return launch_gemm2_t<BN, kEpiStoreF32>(ta, tb, p, grid, stream);
+    default:
+      return cudaErrorInvalidValue;
+  }
 }
 
 template <int BN>
@@ -345,24 +566,34 @@ static cudaError_t dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMa
   }
 }
 
-// Picks the N tile by the fraction of SM slots the tiles fill (waves rounded up), weighted by how
-// well each tile width keeps the tensor core fed from shared memory (128x256 best). 192 exists for
-// the D=768 projections: 768 = 4 x 192 gives one nearly full wave at M=4096 where 256 leaves a
-// third of the SMs idle.
-int gemm_pick_bn(int M, int N, int sm_count) {
-  const long m_blocks = (M + kGemmBM - 1) / kGemmBM;
-  const int candidates[3] = {256, 192, 128};
-  const double intensity[3] = {1.0, 0.97, 0.85};
+constexpr int kTilePair = 0x10000;  // tile code flag: 2-SM (CTA pair) variant
+
+// Picks the tile: the fraction of SM slots the tiles fill (waves rounded up) weighted by how well
+// the tile shape keeps the tensor core fed (operand bytes per MMA work; the 2-SM pair loads 1.5x
+// fewer bytes per FLOP and runs a deeper ring). 192-wide tiles exist for the D=768 projections:
+// 768 = 4 x 192 fills a wave at M=4096 where 256-wide tiles leave a third of the SMs idle.
+int gemm_pick_tile(int M, int N, int sm_count) {
+  struct Cand {
+    int code;
+    int bn;
+    int rows;
+    int slots;
+    double intensity;
+  };
+  const Cand cands[5] = {{kTilePair | 256, 256, 256, sm_count / 2, 1.15},
+                         {kTilePair | 192, 192, 256, sm_count / 2, 1.12},
+                         {256, 256, kGemmBM, sm_count, 1.0},
+                         {192, 192, kGemmBM, sm_count, 0.97},
+                         {128, 128, kGemmBM, sm_count, 0.85}};
   int best = 128;
   double best_score = -1.0;
-  for (int i = 0; i < 3; ++i) {
-    const int bn = candidates[i];
-    if (bn != 128 && N % bn != 0) continue;
-    const long tiles = m_blocks * ((N + bn - 1) / bn);
-    const long waves = (tiles + sm_count - 1) / sm_count;
-    const double score = intensity[i] * static_cast<double>(tiles) / static_cast<double>(waves * sm_count);
+  for (const Cand& c : cands) {
+    if (c.bn != 128 && N % c.bn != 0) continue;
+    const long tiles = static_cast<long>((M + c.rows - 1) / c.rows) * ((N + c.bn - 1) / c.bn);
+    const long waves = (tiles + c.slots - 1) / c.slots;
+    const double score = c.intensity * static_cast<double>(tiles) / static_cast<double>(waves * c.slots);
     if (score > best_score + 1e-9) {
-      best = bn;
+      best = c.code;
       best_score = score;
     }
   }
@@ -370,16 +601,18 @@ int gemm_pick_bn(int M, int N, int sm_count) {
 }
 
 cudaError_t launch_gemm(const __nv_bfloat16* A, const __nv_bfloat16* W, const __nv_bfloat16* bias, int64_t M,
-                        int64_t N, int64_t K, int epi, void* out, int64_t ldo, const uint8_t* row_mask, int bn,
+                        int64_t N, int64_t K, int epi, void* out, int64_t ldo, const uint8_t* row_mask, int tile,
                         cudaStream_t stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   const int sms = device_sm_count(dev);
-  if (bn == 0) bn = gemm_pick_bn(static_cast<int>(M), static_cast<int>(N), sms);
+  if (tile == 0) tile = gemm_pick_tile(static_cast<int>(M), static_cast<int>(N), sms);
+  const bool pair = (tile & kTilePair) != 0;
+  const int bn = tile & 0xFFFF;
   CUtensorMap ta, tb;
   cudaError_t e = make_tmap_bf16_2d(&ta, A, K, M, K * 2, kGemmBK, kGemmBM);
   if (e != cudaSuccess) return e;
-  e = make_tmap_bf16_2d(&tb, W, K, N, K * 2, kGemmBK, bn);
+  e = make_tmap_bf16_2d(&tb, W, K, N, K * 2, kGemmBK, pair ? bn / 2 : bn);
   if (e != cudaSuccess) return e;
   GemmParams p;
   p.out = out;
@@ -392,6 +625,14 @@ cudaError_t launch_gemm(const __nv_bfloat16* A, const __nv_bfloat16* W, const __
   p.m_blocks = static_cast<int>((M + kGemmBM - 1) / kGemmBM);
   p.n_blocks = static_cast<int>((N + bn - 1) / bn);
   p.k_blocks = static_cast<int>((K + kGemmBK - 1) / kGemmBK);
+  if (pair) {
+    const long tiles = static_cast<long>((M + 255) / 256) * p.n_blocks;
+    const long pairs = tiles < sms / 2 ? tiles : sms / 2;
+    const int grid = static_cast<int>(2 * pairs);
+    if (bn == 256) return dispatch_epi2<256>(epi, ta, tb, p, grid, stream);
+    if (bn == 192) return dispatch_epi2<192>(epi, ta, tb, p, grid, stream);
+    return cudaErrorInvalidValue;
+  }
   const long tiles = static_cast<long>(p.m_blocks) * p.n_blocks;
   const int grid = static_cast<int>(tiles < sms ? tiles : sms);
   if (bn == 256) return dispatch_epi<256>(epi, ta, tb, p, grid, stream);

@@ -24,6 +24,8 @@ __global__ void __launch_bounds__(kLnWarpsPerBlock * 32)
     layernorm_vec_kernel(const void* __restrict__ x_, const __nv_bfloat16* __restrict__ gamma,
                          const __nv_bfloat16* __restrict__ beta, float eps, __nv_bfloat16* __restrict__ y,
                          float* __restrict__ resid_out, const uint8_t* __restrict__ row_mask, int64_t rows) {
+  pdl_wait_previous_grid();
+  pdl_allow_next_grid();
   constexpr int D = NV * 128;
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kLnWarpsPerBlock + (threadIdx.x >> 5);
@@ -110,6 +112,8 @@ __global__ void __launch_bounds__(kLnWarpsPerBlock * 32)
                          const __nv_bfloat16* __restrict__ beta, float eps, __nv_bfloat16* __restrict__ y,
                          float* __restrict__ resid_out, const uint8_t* __restrict__ row_mask, int64_t rows,
                          int64_t D) {
+  pdl_wait_previous_grid();
+  pdl_allow_next_grid();
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kLnWarpsPerBlock + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -155,6 +159,8 @@ __global__ void __launch_bounds__(kLnWarpsPerBlock * 32)
                              const __nv_bfloat16* __restrict__ bias, const uint8_t* __restrict__ row_mask,
                              const __nv_bfloat16* __restrict__ gamma, const __nv_bfloat16* __restrict__ beta,
                              float eps, __nv_bfloat16* __restrict__ y, int64_t rows) {
+  pdl_wait_previous_grid();
+  pdl_allow_next_grid();
   constexpr int D = NV * 128;
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kLnWarpsPerBlock + (threadIdx.x >> 5);
@@ -242,9 +248,8 @@ static cudaError_t launch_add_layernorm_t(float* resid, const float* delta, cons
   const dim3 grid(static_cast<unsigned>((rows + kLnWarpsPerBlock - 1) / kLnWarpsPerBlock));
 #define B2_ALN_CASE(NV)                                                                                          \
   case NV:                                                                                                       \
-    add_layernorm_vec_kernel<NV, kZeroRows, kZeroY>                                                              \
-        <<<grid, block, 0, stream>>>(resid, delta, bias, row_mask, gamma, beta, eps, y, rows);                   \
-    return cudaGetLastError();
+    return launch_pdl(add_layernorm_vec_kernel<NV, kZeroRows, kZeroY>, grid, block, 0, stream, resid, delta, bias, \
+                      row_mask, gamma, beta, eps, y, rows);
   switch (D / 128) {
     B2_ALN_CASE(1)
     B2_ALN_CASE(2)
@@ -293,9 +298,8 @@ static cudaError_t launch_layernorm_t(const void* x, const __nv_bfloat16* gamma,
                        (resid_out == nullptr || reinterpret_cast<uintptr_t>(resid_out) % 16 == 0);
 #define B2_LN_CASE(NV)                                                                                   \
   case NV:                                                                                               \
-    layernorm_vec_kernel<NV, kInBf16><<<grid, block, 0, stream>>>(x, gamma, beta, eps, y, resid_out, row_mask, \
-                                                                  rows);                                 \
-    return cudaGetLastError();
+    return launch_pdl(layernorm_vec_kernel<NV, kInBf16>, grid, block, 0, stream, x, gamma, beta, eps, y, resid_out, \
+                      row_mask, rows);
   if (aligned && D % 128 == 0) {
     switch (D / 128) {
       B2_LN_CASE(1)
@@ -316,8 +320,8 @@ static cudaError_t launch_layernorm_t(const void* x, const __nv_bfloat16* gamma,
     }
   }
 #undef B2_LN_CASE
-  layernorm_any_kernel<kInBf16><<<grid, block, 0, stream>>>(x, gamma, beta, eps, y, resid_out, row_mask, rows, D);
-  return cudaGetLastError();
+  return launch_pdl(layernorm_any_kernel<kInBf16>, grid, block, 0, stream, x, gamma, beta, eps, y, resid_out, row_mask,
+                    rows, D);
 }
 
 cudaError_t launch_layernorm(const void* x, int x_is_bf16, const __nv_bfloat16* gamma, const __nv_bfloat16* beta,
