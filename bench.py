@@ -63,6 +63,8 @@ def parse_args(argv=None):
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--workload", default="c2", choices=sorted(BASELINE_CONFIGS))
     p.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    p.add_argument("--collective", default="auto", choices=("auto", "multimem", "nccl"),
+                   help="tensor-parallel reduction: fused into the GEMMs over NVLS multicast, or NCCL all-reduce")
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
     p.add_argument("--cpu-seconds", type=float, default=15.0, help="target CPU time of the CPU baseline sample")
     return p.parse_args(argv)
@@ -283,7 +285,7 @@ def main() -> None:
         from tiktoktechjam2026track3_b200.sharding import TensorParallelTransformer
 
         full = UserOptimizedTransformer(cfg)
-        model = TensorParallelTransformer(cfg, full.state_dict(), device)
+        model = TensorParallelTransformer(cfg, full.state_dict(), device, collective=args.collective)
         del full
         x, mask = generate_random_case(cfg, device, torch.bfloat16, 100000, pad)
     else:
@@ -447,25 +449,34 @@ def main() -> None:
                 "layers": cfg.num_layers,
                 "causal": cfg.causal,
                 "padding_ratio": pad,
-                "parallelism": (f"tp{world} (heads / FFN columns, 2 NCCL all-reduces of the fp32 [T, D] partial "
-                                "per block)") if tensor_parallel else f"dp{world} (batch shards, no collective)",
+                "parallelism": (f"tp{world} (heads / FFN columns; " + (
+                    "out_proj / ffn_out GEMM epilogues add their partial tiles into every GPU's fp32 residual "
+                    "with multimem.red over NVSwitch, 4 flag barriers per block)" if model.collective == "multimem"
+                    else "2 NCCL all-reduces of the fp32 [T, D] partial per block)"))
+                if tensor_parallel else f"dp{world} (batch shards, no collective)",
                 "l2": "flushed (256 MiB write) before every timed step",
-                "launches": ("eager launches + NCCL all-reduce" if tensor_parallel else
+                "launches": (f"eager launches ({model.collective})" if tensor_parallel else
                              "first/final LayerNorm eager, the block launches replayed from a CUDA graph"),
             },
             "roofline": roofline,
             "kernels": kernels,
             "model_flops_per_step": total_flops * world,
             "allreduce_ms_per_step": kind_ms.get("allreduce", 0.0),
+            "barrier_ms_per_step": kind_ms.get("barrier", 0.0),
+            "ms_per_step_by_launch_kind": {k: round(v, 4) for k, v in sorted(kind_ms.items())},
             "mfu_of_bf16_peak": mfu,
             "cpu_baseline": cpu,
             "e2e": {"value": tokens_per_step / (e2e_per_step / 1e3), "unit": UNIT, "ms_per_step": e2e_per_step,
                     "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world},
-            "gpu_launches": args.steps * UserOptimizedTransformer.launches_per_forward(cfg.num_layers),
+            "gpu_launches": args.steps * (model.launches_per_forward(cfg.num_layers) if tensor_parallel else
+                                          UserOptimizedTransformer.launches_per_forward(cfg.num_layers)),
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
     if dist is not None:
+        torch.cuda.synchronize()
+        if tensor_parallel:
+            model.close()
         dist.barrier()
         dist.destroy_process_group()
 

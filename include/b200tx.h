@@ -41,6 +41,12 @@ extern "C" {
 #define B2_EPI_RESIDUAL 2       /* out f32 (in place) = mask ? out + acc + bias : out    */
 #define B2_EPI_RESIDUAL_ZERO 3  /* out f32 (in place) = mask ? out + acc + bias : 0      */
 #define B2_EPI_STORE_F32 4      /* out f32 = acc (+ bias if non-null)                     */
+/* Tensor parallel with the all-reduce fused into the GEMM: `out` is the NVLS multicast address of a
+ * replicated fp32 residual [m, ldo] (e.g. torch symmetric memory's multicast_ptr); each rank's
+ * partial acc (+ bias, passed on one rank only) is added into every GPU's copy with multimem.red
+ * as tiles finish. The caller orders other reads/writes of the residual with cross-GPU barriers. */
+#define B2_EPI_MC_RESIDUAL 5       /* every copy: kept rows += acc + bias                   */
+#define B2_EPI_MC_RESIDUAL_ZERO 6  /* every copy: kept rows += acc + bias, masked rows = 0  */
 
 /* b2_linear_fwd tile_n flag: the 2-SM variant (a CTA pair computes 256-row tiles with
  * tcgen05.mma.cta_group::2), combined with an N tile of 192 or 256. */
@@ -110,6 +116,19 @@ int b2_linear_fwd(const void* a, const void* w, const void* bias, int64_t m, int
 int b2_attention_fwd(const void* qkv, int64_t ld_qkv, int64_t q_col, int64_t k_col, int64_t v_col, int64_t batch,
                      int64_t seq_len, int64_t num_heads, int64_t head_dim, const int32_t* kv_len, int causal,
                      float scale, void* ctx, int64_t ld_ctx, void* stream);
+
+/*
+ * Cross-GPU barrier for tensor-parallel runs whose all-reduce is fused into the GEMM epilogues
+ * (B2_EPI_MC_RESIDUAL*). No counterpart in the reference, which runs on one GPU; in this build
+ * it takes the place of the synchronisation an NCCL all-reduce gives.
+ *   pads    host array of `world` device pointers: every rank's flag pad (4 x 8 uint32, zeroed
+ *           before first use) as mapped into this process (e.g. symmetric memory buffer_ptrs)
+ *   channel 0..3; ranks must use channels in the same order
+ * Enqueues one block on `stream` that signals every peer and waits for every peer's signal
+ * (release/acquire at system scope). A wait that exceeds 4 s records a status for
+ * b2_device_status() instead of hanging. world == 1 is a no-op.
+ */
+int b2_peer_barrier(void* const* pads, int world, int rank, int channel, void* stream);
 
 #ifdef __cplusplus
 }

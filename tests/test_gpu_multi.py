@@ -1,7 +1,8 @@
 """Multi-GPU plans on B200s (needs 2+ GPUs; skipped otherwise): one process per GPU over NCCL.
 
-* tensor parallel (heads/FFN columns, NCCL all-reduce) agrees with the single-GPU model within the
-  parity gate (reduction order differs, so not bitwise);
+* tensor parallel (heads/FFN columns) agrees with the single-GPU model within the parity gate
+  (reduction order differs, so not bitwise), both with the reduction fused into the GEMM
+  epilogues over NVLS multicast (where the GPUs support it) and with the NCCL all-reduce;
 * a batch shard on rank r is bit-identical to the same sequences of the single-GPU run.
 """
 
@@ -17,7 +18,7 @@ import torch.multiprocessing as mp
 from oracle import reference_fp32 as oracle
 from tiktoktechjam2026track3_b200 import UserOptimizedTransformer, baseline_gate
 from tiktoktechjam2026track3_b200.cases import TransformerConfig
-from tiktoktechjam2026track3_b200.sharding import TensorParallelTransformer, batch_shard
+from tiktoktechjam2026track3_b200.sharding import TensorParallelTransformer, batch_shard, multicast_supported
 
 pytestmark = pytest.mark.gpu
 
@@ -40,16 +41,34 @@ def _worker(rank, world, port, cfg, pad, q):
         model = UserOptimizedTransformer(cfg)
         model.load_state_dict(state, strict=True)
         model = model.to(device=dev, dtype=torch.bfloat16).eval()
-        tp = TensorParallelTransformer(cfg, state, dev)
+        collectives = ["nccl"] + (["multimem"] if multicast_supported(dev) else [])
         with torch.inference_mode():
             single = model(xb, mask)
-            tp_out = tp(xb, mask)
             b0, b1 = batch_shard(cfg.batch_size, world, rank)
             shard = model(xb[b0:b1].contiguous(), mask[b0:b1].contiguous())
+            outs = {}
+            for coll in collectives:
+                tp = TensorParallelTransformer(cfg, state, dev, collective=coll)
+                outs[coll] = tp(xb, mask)
+                outs[coll + "_again"] = tp(xb * 0.5, mask)
+                outs[coll + "_again_ref"] = model(xb * 0.5, mask)
+                torch.cuda.synchronize()
+                tp.close()
+                dist.barrier()
         torch.cuda.synchronize()
-        gate = baseline_gate(tp_out, single.float())
-        q.put((rank, gate.passed, gate.normwise_error, bool(torch.equal(shard, single[b0:b1]))))
+        from tiktoktechjam2026track3_b200 import _capi
+
+        status = _capi.device_status(clear=True)
+        result = {"rank": rank, "status": status, "shard_equal": bool(torch.equal(shard, single[b0:b1])),
+                  "collectives": collectives}
+        for coll in collectives:
+            g = baseline_gate(outs[coll], single.float())
+            g2 = baseline_gate(outs[coll + "_again"], outs[coll + "_again_ref"].float())
+            result[coll] = (g.passed and g2.passed, g.normwise_error, g2.normwise_error,
+                            bool(torch.all(outs[coll][~mask] == 0)))
+        q.put(result)
     finally:
+        dist.barrier()
         dist.destroy_process_group()
 
 
@@ -69,6 +88,9 @@ def test_tensor_parallel_and_batch_shards_on_two_gpus(cuda_device, pad):
         p.join(timeout=300)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     results = [q.get(timeout=5) for _ in range(world)]
-    for rank, passed, err, shard_equal in results:
-        assert passed, (rank, err)
-        assert shard_equal, rank
+    for r in results:
+        assert r["status"] == 0, r
+        assert r["shard_equal"], r
+        for coll in r["collectives"]:
+            assert r[coll][0], (coll, r)
+            assert r[coll][3], (coll, r)  # padding rows are zero

@@ -26,6 +26,9 @@ EPI_BIAS_GELU = 1
 EPI_RESIDUAL = 2
 EPI_RESIDUAL_ZERO = 3
 EPI_STORE_F32 = 4
+EPI_MC_RESIDUAL = 5
+EPI_MC_RESIDUAL_ZERO = 6
+TILE_PAIR = 0x10000
 
 # Every symbol include/b200tx.h declares, with its ctypes signature.
 _i64 = ctypes.c_int64
@@ -50,6 +53,7 @@ SIGNATURES = {
         ctypes.c_int,
         [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, ctypes.c_int, ctypes.c_float, _vp, _i64, _vp],
     ),
+    "b2_peer_barrier": (ctypes.c_int, [ctypes.POINTER(_vp), ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
 }
 
 _lock = threading.Lock()
@@ -184,11 +188,17 @@ def linear(
     w: torch.Tensor,
     bias: Optional[torch.Tensor],
     epilogue: int,
-    out: torch.Tensor,
+    out: Optional[torch.Tensor],
     row_mask: Optional[torch.Tensor] = None,
     tile_n: int = 0,
+    out_ptr: Optional[int] = None,
+    out_ld: Optional[int] = None,
 ) -> None:
-    """out = epilogue(a @ w.T + bias) (see b2_linear_fwd)."""
+    """out = epilogue(a @ w.T + bias) (see b2_linear_fwd).
+
+    For the multicast epilogues (EPI_MC_*) pass `out_ptr` (an NVLS multicast address of an fp32
+    [m, out_ld] buffer) and `out_ld` instead of `out`.
+    """
     _require(a, torch.bfloat16, "a")
     _require(w, torch.bfloat16, "w")
     m, k = a.shape[0] if a.dim() == 2 else a.numel() // a.shape[-1], a.shape[-1]
@@ -197,15 +207,20 @@ def linear(
         raise ValueError(f"w has shape {tuple(w.shape)}, expected [n, {k}]")
     if bias is not None:
         _require(bias, torch.bfloat16, "bias")
-    out_dtype = torch.bfloat16 if epilogue in (EPI_BIAS, EPI_BIAS_GELU) else torch.float32
-    _require(out, out_dtype, "out")
-    if out.numel() < m * n:
-        raise ValueError("out is too small")
-    ldo = out.shape[-1]
+    if epilogue in (EPI_MC_RESIDUAL, EPI_MC_RESIDUAL_ZERO):
+        if out is not None or out_ptr is None or out_ld is None:
+            raise ValueError("multicast epilogues take out_ptr and out_ld (and no out tensor)")
+        dst, ldo = int(out_ptr), int(out_ld)
+    else:
+        out_dtype = torch.bfloat16 if epilogue in (EPI_BIAS, EPI_BIAS_GELU) else torch.float32
+        _require(out, out_dtype, "out")
+        if out.numel() < m * n:
+            raise ValueError("out is too small")
+        dst, ldo = out.data_ptr(), out.shape[-1]
     if row_mask is not None:
         _require(row_mask, torch.uint8, "row_mask")
     status = load_library().b2_linear_fwd(
-        _ptr(a), _ptr(w), _ptr(bias), m, n, k, int(epilogue), _ptr(out), ldo, _ptr(row_mask), int(tile_n),
+        _ptr(a), _ptr(w), _ptr(bias), m, n, k, int(epilogue), dst, ldo, _ptr(row_mask), int(tile_n),
         _stream_ptr(a.device),
     )
     _check(status, "b2_linear_fwd")
@@ -237,3 +252,16 @@ def attention(
         1 if causal else 0, float(scale), _ptr(ctx), ctx.shape[-1], _stream_ptr(qkv.device),
     )
     _check(status, "b2_attention_fwd")
+
+
+PAD_WORDS = 32  # kPadChannels x kMaxPeers uint32 flags per rank
+
+
+def peer_barrier(pads, rank: int, channel: int, device: torch.device) -> None:
+    """Enqueues a cross-GPU barrier on the current stream (see b2_peer_barrier).
+
+    `pads` lists every rank's flag-pad device address (ints) as mapped into this process.
+    """
+    arr = (_vp * len(pads))(*[int(p) for p in pads])
+    status = load_library().b2_peer_barrier(arr, len(pads), int(rank), int(channel), _stream_ptr(device))
+    _check(status, "b2_peer_barrier")

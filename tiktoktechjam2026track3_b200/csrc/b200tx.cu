@@ -20,6 +20,7 @@
 #include "gemm.cuh"
 #include "attention.cuh"
 #include "attention_pair.cuh"
+#include "peer.cuh"
 
 #define B2_API extern "C" __attribute__((visibility("default")))
 
@@ -133,7 +134,7 @@ B2_API int b2_linear_fwd(const void* a, const void* w, const void* bias, int64_t
   if (a == nullptr || w == nullptr || out == nullptr) return fail(1, "b2_linear_fwd: null pointer argument");
   if (m < 0 || n <= 0 || k <= 0) return fail(1, "b2_linear_fwd: invalid shape m=%lld n=%lld k=%lld", (long long)m,
                                              (long long)n, (long long)k);
-  if (epilogue < 0 || epilogue > 4) return fail(1, "b2_linear_fwd: unknown epilogue %d", epilogue);
+  if (epilogue < 0 || epilogue > 6) return fail(1, "b2_linear_fwd: unknown epilogue %d", epilogue);
   if (n % 32 != 0) return fail(2, "b2_linear_fwd: n=%lld must be a multiple of 32", (long long)n);
   if (k % 8 != 0) return fail(2, "b2_linear_fwd: k=%lld must be a multiple of 8", (long long)k);
   if (ldo < n || ldo % 8 != 0) return fail(2, "b2_linear_fwd: ldo=%lld must be >= n and a multiple of 8", (long long)ldo);
@@ -202,4 +203,21 @@ B2_API int b2_add_layernorm_fwd(float* resid, const float* delta, const void* bi
                                            static_cast<__nv_bfloat16*>(y), rows, d_model,
                                            static_cast<cudaStream_t>(stream)),
                       "b2_add_layernorm_fwd");
+}
+
+B2_API int b2_peer_barrier(void* const* pads, int world, int rank, int channel, void* stream) {
+  if (pads == nullptr) return fail(1, "b2_peer_barrier: pads is null");
+  if (world < 1 || world > kMaxPeers) return fail(2, "b2_peer_barrier: world=%d not in [1, %d]", world, kMaxPeers);
+  if (rank < 0 || rank >= world) return fail(1, "b2_peer_barrier: rank %d outside world %d", rank, world);
+  if (channel < 0 || channel >= kPadChannels)
+    return fail(1, "b2_peer_barrier: channel %d not in [0, %d)", channel, kPadChannels);
+  PeerPads p{};
+  for (int r = 0; r < world; ++r) {
+    if (pads[r] == nullptr || (reinterpret_cast<uintptr_t>(pads[r]) & 3u))
+      return fail(1, "b2_peer_barrier: pad of rank %d is null or misaligned", r);
+    p.pad[r] = static_cast<uint32_t*>(pads[r]);
+  }
+  if (world == 1) return 0;
+  return check_launch(launch_peer_barrier(p, world, rank, channel, static_cast<cudaStream_t>(stream)),
+                      "b2_peer_barrier");
 }

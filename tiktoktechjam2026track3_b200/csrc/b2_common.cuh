@@ -24,6 +24,7 @@ enum : uint32_t {
   kKernelLayerNorm = 1,
   kKernelGemm = 2,
   kKernelAttention = 3,
+  kKernelPeerBarrier = 4,
 };
 enum : uint32_t {
   kReasonTimeout = 1,
@@ -502,6 +503,22 @@ __device__ __forceinline__ uint64_t make_sdesc_sw128(uint32_t smem_addr, uint32_
 // ---------------------------------------------------------------------------------------------
 __device__ __forceinline__ void pdl_wait_previous_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_allow_next_grid() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------------------------
+// NVLink SHARP (NVLS) multicast memory: one operation on a multicast address reaches the same
+// offset of every GPU's copy through the NVSwitch.
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ void multimem_red_add_v4(float* mc, float a, float b, float c, float d) {
+  asm volatile("multimem.red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "f"(a), "f"(b),
+               "f"(c), "f"(d)
+               : "memory");
+}
+__device__ __forceinline__ void multimem_st_v4(float* mc, float a, float b, float c, float d) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------------------------
 // Small numeric helpers

@@ -9,6 +9,13 @@
 //   kEpiResidual      res_f32  = mask ? res + acc + bias : res           (out_proj, masked_fill :78-79, x + a :733)
 //   kEpiResidualZero  res_f32  = mask ? res + acc + bias : 0             (ffn_out, x + f :734, masked_fill :736-737)
 //   kEpiStoreF32      out_f32  = acc (+ bias when given)                 (tensor-parallel partial sums)
+//   kEpiMcResidual    res_f32 += acc (+ bias) on every GPU, kept rows     (tensor parallel, fused all-reduce)
+//   kEpiMcResidualZero  same, and masked rows set to 0 on every GPU
+// The two kEpiMc* epilogues take `out` as an NVLS multicast address of the replicated fp32
+// residual: each rank's partial tile is added into every rank's copy by multimem.red through the
+// NVSwitch while the rest of the GEMM still runs, so the reduction needs no separate collective.
+// The caller passes the bias on one rank only and orders reads of the residual with cross-GPU
+// barriers before and after the GEMM.
 // A is [M, K] row-major bf16 (tokens x features), W is [N, K] row-major bf16 (nn.Linear layout,
 // i.e. K-major for the B operand), the residual stream is fp32 [M, ldo].
 //
@@ -34,6 +41,8 @@ enum GemmEpilogue : int {
   kEpiResidual = 2,
   kEpiResidualZero = 3,
   kEpiStoreF32 = 4,
+  kEpiMcResidual = 5,
+  kEpiMcResidualZero = 6,
 };
 
 struct GemmParams {
@@ -60,6 +69,24 @@ struct GemmCfg {
   static constexpr int kTmemCols = 2 * kAccStride;          // a power of two, as tcgen05.alloc requires
   static constexpr int kBarrierBytes = 256;
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes;
+};
+
+template <int EPI>
+__host__ __device__ constexpr bool is_mc_epi() {
+  return EPI == kEpiMcResidual || EPI == kEpiMcResidualZero;
+}
+// The multicast epilogues transpose each warp's 32 x 32 fp32 chunk through shared memory so that
+// every multimem instruction covers whole 128-byte row segments (8 lanes x 16 B per row) instead
+// of 32 scattered 16-byte pieces: NVLink carries reductions as separate requests, and 16-byte
+// requests leave most of the link idle.
+constexpr int kMcStageBytes = (kGemmThreads / 32 - 2) * 32 * 32 * 4;
+
+template <int BN, int EPI>
+struct GemmSmem {
+  static constexpr int kStages = (is_mc_epi<EPI>() && BN == 192) ? 4 : GemmCfg<BN>::kStages;
+  static constexpr int kEpiBytes = is_mc_epi<EPI>() ? kMcStageBytes : 0;
+  static constexpr int kBytes = kStages * GemmCfg<BN>::kStageBytes + 1024 + GemmCfg<BN>::kBarrierBytes + kEpiBytes;
+  static_assert(kBytes <= 232448, "shared memory per CTA");
 };
 
 __device__ __forceinline__ void load_bias32(const __nv_bfloat16* bias, int col0, float (&b)[32]) {
@@ -127,6 +154,42 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmParams& p, int row
   }
 }
 
+// Multicast epilogue of one warp's 32 rows x 32 columns (row0 = the warp's first row; lane i
+// holds row row0 + i in acc). Whole warp participates.
+template <int EPI>
+__device__ __forceinline__ void mc_epilogue_chunk(const GemmParams& p, int row0, int col0, const float (&acc)[32],
+                                                  float4* stage) {
+  const int lane = threadIdx.x & 31;
+  // Row `lane` as 8 float4 chunks, chunk index XOR-swizzled by the row so that both the stores
+  // (8 lanes = 8 rows, same chunk) and the loads below (8 lanes = 1 row, 8 chunks) touch all banks.
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    stage[lane * 8 + (c ^ (lane & 7))] = make_float4(acc[4 * c], acc[4 * c + 1], acc[4 * c + 2], acc[4 * c + 3]);
+  __syncwarp();
+  const int q = lane & 7;
+  float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (p.bias != nullptr) {
+    const uint2 raw = *reinterpret_cast<const uint2*>(p.bias + col0 + 4 * q);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+    b = make_float4(__low2float(h[0]), __high2float(h[0]), __low2float(h[1]), __high2float(h[1]));
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = i * 4 + (lane >> 3);
+    const int row = row0 + r;
+    const float4 v = stage[r * 8 + (q ^ (r & 7))];
+    if (row < p.M) {
+      float* dst = static_cast<float*>(p.out) + static_cast<int64_t>(row) * p.ldo + col0 + 4 * q;
+      const bool keep = (p.row_mask == nullptr) || (p.row_mask[row] != 0);
+      if (keep)
+        multimem_red_add_v4(dst, v.x + b.x, v.y + b.y, v.z + b.z, v.w + b.w);
+      else if constexpr (EPI == kEpiMcResidualZero)
+        multimem_st_v4(dst, 0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  __syncwarp();
+}
+
 // Waits for a phase without looking at the abort flag (used only on the abort path, to let
 // copies and MMAs that are still in flight land before the CTA releases its memory).
 __device__ __forceinline__ void mbar_drain_wait(uint64_t* bar, uint32_t parity) {
@@ -141,7 +204,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                    const GemmParams p) {
   using Cfg = GemmCfg<BN>;
-  constexpr int kStages = Cfg::kStages;
+  constexpr int kStages = GemmSmem<BN, EPI>::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* s_a = smem;
@@ -273,6 +336,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int quad = warp & 3;
     const int half = (warp - 2) >> 2;
     const int row_in_tile = quad * 32 + lane;
+    float4* epi_stage = reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(full) + Cfg::kBarrierBytes) + (warp - 2) * 256;
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int m_blk = tile / p.n_blocks;
@@ -290,11 +354,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (col0 >= p.N) break;  // warp-uniform
         float v[32];
         tmem_load_32cols(t_row + c * 32, v);
-        if (row < p.M) gemm_epilogue_chunk<EPI>(p, row, col0, v);
+        if constexpr (is_mc_epi<EPI>())
+          mc_epilogue_chunk<EPI>(p, row - lane, col0, v, epi_stage);
+        else if (row < p.M)
+          gemm_epilogue_chunk<EPI>(p, row, col0, v);
       }
       tc_fence_before_sync();
       mbar_arrive(&acc_empty[acc]);
     }
+    if constexpr (EPI == kEpiMcResidual || EPI == kEpiMcResidualZero) fence_acq_rel_sys();
   }
 
   __syncthreads();
@@ -323,6 +391,10 @@ struct Gemm2Cfg {
   static constexpr int kTmemCols = 512;
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
 };
+template <int BN, int EPI>
+constexpr int gemm2_smem_bytes() {
+  return Gemm2Cfg<BN>::kSmemBytes + (is_mc_epi<EPI>() ? kMcStageBytes : 0);
+}
 
 template <int BN, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
@@ -449,6 +521,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     const int quad = warp & 3;
     const int half = (warp - 2) >> 2;
     const int row_in_tile = static_cast<int>(rank) * 128 + quad * 32 + lane;
+    float4* epi_stage = reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(full) + 256) + (warp - 2) * 256;
     const uint32_t acc_empty_leader0 = cluster_map_to_rank(&acc_empty[0], 0);
     const uint32_t acc_empty_leader1 = cluster_map_to_rank(&acc_empty[1], 0);
     int local = 0;
@@ -468,11 +541,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         if (col0 >= p.N) break;  // warp-uniform
         float v[32];
         tmem_load_32cols(t_row + c * 32, v);
-        if (row < p.M) gemm_epilogue_chunk<EPI>(p, row, col0, v);
+        if constexpr (is_mc_epi<EPI>())
+          mc_epilogue_chunk<EPI>(p, row - lane, col0, v, epi_stage);
+        else if (row < p.M)
+          gemm_epilogue_chunk<EPI>(p, row, col0, v);
       }
       tc_fence_before_sync();
       mbar_arrive_cluster(acc ? acc_empty_leader1 : acc_empty_leader0);
     }
+    if constexpr (EPI == kEpiMcResidual || EPI == kEpiMcResidualZero) fence_acq_rel_sys();
   }
 
   if (*abort_flag && threadIdx.x == 0) {
@@ -506,10 +583,11 @@ static cudaError_t launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, c
   cudaError_t attr_err = cudaSuccess;
   std::call_once(once[dev & 63], [&] {
     attr_err = cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    Cfg::kSmemBytes);
+                                    GemmSmem<BN, EPI>::kBytes);
   });
   if (attr_err != cudaSuccess) return attr_err;
-  return launch_pdl(gemm_tc_kernel<BN, EPI>, dim3(grid), dim3(kGemmThreads), Cfg::kSmemBytes, stream, ta, tb, p);
+  return launch_pdl(gemm_tc_kernel<BN, EPI>, dim3(grid), dim3(kGemmThreads), GemmSmem<BN, EPI>::kBytes, stream, ta,
+                    tb, p);
 }
 
 template <int BN, int EPI>
@@ -522,10 +600,11 @@ static cudaError_t launch_gemm2_t(const CUtensorMap& ta, const CUtensorMap& tb, 
   cudaError_t attr_err = cudaSuccess;
   std::call_once(once[dev & 63], [&] {
     attr_err = cudaFuncSetAttribute(gemm_tc2_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    Cfg::kSmemBytes);
+                                    gemm2_smem_bytes<BN, EPI>());
   });
   if (attr_err != cudaSuccess) return attr_err;
-  return launch_pdl(gemm_tc2_kernel<BN, EPI>, dim3(grid), dim3(kGemmThreads), Cfg::kSmemBytes, stream, ta, tb, p);
+  return launch_pdl(gemm_tc2_kernel<BN, EPI>, dim3(grid), dim3(kGemmThreads), gemm2_smem_bytes<BN, EPI>(), stream,
+                    ta, tb, p);
 }
 
 template <int BN>
@@ -542,6 +621,10 @@ static cudaError_t dispatch_epi2(int epi, const CUtensorMap& ta, const CUtensorM
       return launch_gemm2_t<BN, kEpiResidualZero>(ta, tb, p, grid, stream);
     case kEpiStoreF32:
       return launch_gemm2_t<BN, kEpiStoreF32>(ta, tb, p, grid, stream);
+    case kEpiMcResidual:
+      return launch_gemm2_t<BN, kEpiMcResidual>(ta, tb, p, grid, stream);
+    case kEpiMcResidualZero:
+      return launch_gemm2_t<BN, kEpiMcResidualZero>(ta, tb, p, grid, stream);
     default:
       return cudaErrorInvalidValue;
   }
@@ -561,6 +644,10 @@ static cudaError_t dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMa
       return launch_gemm_t<BN, kEpiResidualZero>(ta, tb, p, grid, stream);
     case kEpiStoreF32:
       return launch_gemm_t<BN, kEpiStoreF32>(ta, tb, p, grid, stream);
+    case kEpiMcResidual:
+      return launch_gemm_t<BN, kEpiMcResidual>(ta, tb, p, grid, stream);
+    case kEpiMcResidualZero:
+      return launch_gemm_t<BN, kEpiMcResidualZero>(ta, tb, p, grid, stream);
     default:
       return cudaErrorInvalidValue;
   }

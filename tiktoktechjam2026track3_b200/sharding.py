@@ -12,9 +12,17 @@ are this build's own, one process per GPU with torch.distributed (NCCL) for the 
   columns are split across ranks (Megatron-style). Rank r owns heads [r*H/n, (r+1)*H/n): rows of
   q/k/v_proj and the matching columns of out_proj; and FFN columns [r*F/n, (r+1)*F/n): rows of
   ffn_in and columns of ffn_out. LayerNorms are replicated. Each residual sub-block ends in a
-  per-rank fp32 partial sum [T, D] that is all-reduced over NCCL (two all-reduces per block, one
-  per residual sub-block); the biases of out_proj/ffn_out are added once, after the reduction,
-  in the fused residual + LayerNorm kernel (b2_add_layernorm_fwd).
+  per-rank partial sum [T, D] that has to be summed over ranks, one reduction per residual
+  sub-block. Two ways to do it (`collective=`):
+
+  - "multimem" (default where the GPUs support NVLink SHARP multicast): the fp32 residual stream
+    is replicated in symmetric memory, and the out_proj / ffn_out GEMMs add their partial tiles
+    (plus the bias, on rank 0 only) straight into every rank's copy with multimem.red through the
+    NVSwitch (B2_EPI_MC_RESIDUAL*), tile by tile while the GEMM runs. The reduction and the
+    residual add happen inside the GEMM; four cross-GPU flag barriers per layer (b2_peer_barrier)
+    order the residual's readers (LayerNorms) against the adds.
+  - "nccl": each GEMM writes an fp32 partial, NCCL all-reduces it, and the fused residual +
+    LayerNorm kernel (b2_add_layernorm_fwd) adds it with the bias. Kept as the baseline.
 """
 
 from __future__ import annotations
@@ -87,7 +95,8 @@ class TensorParallelTransformer:
     output. Built from the full model's state dict (reference key names).
     """
 
-    def __init__(self, config, state: Dict[str, torch.Tensor], device: torch.device, group=None) -> None:
+    def __init__(self, config, state: Dict[str, torch.Tensor], device: torch.device, group=None,
+                 collective: str = "auto") -> None:
         import torch.distributed as dist
 
         self.config = config_from(config)
@@ -104,6 +113,14 @@ class TensorParallelTransformer:
         self.eps = 1e-5
         self._mask_lengths = MaskLengths()
         self._launch_log: Optional[list] = None
+        if collective == "auto":
+            collective = "multimem" if multicast_supported(device) and self.world > 1 else "nccl"
+        if collective not in ("multimem", "nccl"):
+            raise ValueError(f"collective must be 'auto', 'multimem' or 'nccl', not {collective!r}")
+        if collective == "multimem" and not multicast_supported(device):
+            raise RuntimeError("collective='multimem' needs NVLink SHARP multicast (symmetric memory) support")
+        self.collective = collective
+        self._symm: Optional[Tuple[int, torch.Tensor, object, int, List[int]]] = None
 
     def record_launches(self, enabled: bool) -> None:
         """When enabled, every kernel launch and all-reduce is bracketed by CUDA events."""
@@ -131,7 +148,89 @@ class TensorParallelTransformer:
 
         dist.all_reduce(t, group=self.group)
 
+    def _symmetric_residual(self, tokens: int, d: int):
+        """fp32 residual [tokens, d] in symmetric memory plus the ranks' barrier pads.
+
+        Returns (resid, multicast address of resid, every rank's pad address). Allocated by a
+        collective rendezvous the first time a token count is seen, then reused.
+        """
+        if self._symm is not None and self._symm[0] == tokens:
+            return self._symm[1], self._symm[3], self._symm[4]
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self._symm = None
+        words = tokens * d + 64  # the pad sits after the residual, 256-byte aligned
+        buf = symm_mem.empty(words, dtype=torch.float32, device=self.device)
+        buf[tokens * d:].zero_()
+        group = self.group if self.group is not None else dist.group.WORLD
+        handle = symm_mem.rendezvous(buf, group)
+        mc = int(handle.multicast_ptr)
+        if mc == 0:
+            raise RuntimeError("symmetric memory has no multicast address on this device")
+        pads = [int(p) + tokens * d * 4 for p in handle.buffer_ptrs]
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # every pad is zero before any rank signals
+        self._symm = (tokens, buf[: tokens * d].view(tokens, d), handle, mc, pads)
+        return self._symm[1], mc, pads
+
+    def _barrier(self, pads: List[int], channel: int) -> None:
+        _capi.peer_barrier(pads, self.rank, channel, self.device)
+
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if self.collective == "multimem":
+            return self._forward_multimem(x, valid_token_mask)
+        return self._forward_nccl(x, valid_token_mask)
+
+    def _forward_multimem(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]) -> torch.Tensor:
+        cfg = self.config
+        if not x.is_cuda or x.dtype != torch.bfloat16:
+            raise RuntimeError("TensorParallelTransformer needs a bf16 CUDA input")
+        batch, seq_len, d = x.shape
+        if valid_token_mask is not None and valid_token_mask.device != x.device:
+            raise ValueError("valid_token_mask must be on x's device")
+        kv_len, row_mask = self._mask_lengths(valid_token_mask, batch, seq_len)
+        n = self.world
+        tokens = batch * seq_len
+        h_loc = cfg.num_heads // n
+        hd = cfg.head_dim
+        d_loc = h_loc * hd
+        f_loc = cfg.ffn_dim // n
+        dev = x.device
+        resid, mc, pads = self._symmetric_residual(tokens, d)
+        ln = torch.empty(tokens, d, device=dev, dtype=torch.bfloat16)
+        qkv = torch.empty(tokens, 3 * d_loc, device=dev, dtype=torch.bfloat16)
+        ctx = torch.empty(tokens, d_loc, device=dev, dtype=torch.bfloat16)
+        hidden = torch.empty(tokens, f_loc, device=dev, dtype=torch.bfloat16)
+        out = torch.empty(batch, seq_len, d, device=dev, dtype=torch.bfloat16)
+        x2 = x.contiguous().view(tokens, d)
+        lead = self.rank == 0  # adds the out_proj / ffn_out biases
+        s0 = self.shards[0]
+        t = self._timed
+        t("layernorm", _capi.layernorm, x2, s0["ln1_w"], s0["ln1_b"], self.eps, ln, resid_out=resid)
+        for i, s in enumerate(self.shards):
+            t("gemm_qkv", _capi.linear, ln, s["w_qkv"], s["b_qkv"], _capi.EPI_BIAS, qkv)
+            t("attention", _capi.attention, qkv, batch, seq_len, h_loc, hd, 0, d_loc, 2 * d_loc, kv_len, cfg.causal,
+              hd**-0.5, ctx)
+            t("barrier", self._barrier, pads, 0)  # every rank is done reading its residual copy
+            t("gemm_out", _capi.linear, ctx, s["w_o"], s["b_o"] if lead else None, _capi.EPI_MC_RESIDUAL, None,
+              row_mask, out_ptr=mc, out_ld=d)
+            t("barrier", self._barrier, pads, 1)  # every rank's adds have landed in every copy
+            t("layernorm", _capi.layernorm, resid, s["ln2_w"], s["ln2_b"], self.eps, ln)
+            t("gemm_ffn_in", _capi.linear, ln, s["w_1"], s["b_1"], _capi.EPI_BIAS_GELU, hidden)
+            t("barrier", self._barrier, pads, 2)
+            t("gemm_ffn_out", _capi.linear, hidden, s["w_2"], s["b_2"] if lead else None,
+              _capi.EPI_MC_RESIDUAL_ZERO, None, row_mask, out_ptr=mc, out_ld=d)
+            t("barrier", self._barrier, pads, 3)
+            if i == len(self.shards) - 1:
+                t("layernorm", _capi.layernorm, resid, self.final_w, self.final_b, self.eps, out.view(tokens, d),
+                  row_mask=row_mask)
+            else:
+                nxt = self.shards[i + 1]
+                t("layernorm", _capi.layernorm, resid, nxt["ln1_w"], nxt["ln1_b"], self.eps, ln)
+        return out
+
+    def _forward_nccl(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]) -> torch.Tensor:
         cfg = self.config
         if not x.is_cuda or x.dtype != torch.bfloat16:
             raise RuntimeError("TensorParallelTransformer needs a bf16 CUDA input")
@@ -177,6 +276,24 @@ class TensorParallelTransformer:
 
     __call__ = forward
 
-    @staticmethod
-    def launches_per_forward(num_layers: int) -> int:
-        return 1 + 7 * num_layers
+    def launches_per_forward(self, num_layers: int) -> int:
+        """Kernels of this library per forward (NCCL's own kernels not counted)."""
+        return 1 + (11 if self.collective == "multimem" else 7) * num_layers
+
+    def close(self) -> None:
+        """Drops the symmetric-memory residual (call on every rank before destroying the group)."""
+        self._symm = None
+
+
+def multicast_supported(device: torch.device) -> bool:
+    """True when symmetric memory on `device` has an NVLink SHARP multicast address."""
+    try:
+        from torch._C._distributed_c10d import _SymmetricMemory
+        from torch._C._autograd import DeviceType
+    except ImportError:
+        return False
+    idx = torch.device(device).index or 0
+    try:
+        return bool(_SymmetricMemory.has_multicast_support(DeviceType.CUDA, idx))
+    except RuntimeError:
+        return False
