@@ -96,6 +96,29 @@ def test_gemm_bias_gelu(m, n, k):
     torch.testing.assert_close(out.float(), expect, atol=2e-2, rtol=1e-2)
 
 
+def test_gelu_epilogue_against_exact_gelu():
+    """GELU on exactly representable GEMM outputs (A @ I) against float64 exact-erf GELU.
+
+    The epilogue evaluates erf with a rational-exponential formula (|error| <= 1.5e-7) in fp32,
+    so 0.5 x (1 + erf) keeps fp32's absolute cancellation error (~1e-7 |x|) in the negative tail,
+    as ATen's fp32 GELU does; elsewhere the result is the correctly rounded bf16 value or one ulp
+    away when the exact value sits next to a rounding boundary."""
+    g = _gen(11)
+    m, k = 4096, 64
+    x = (torch.rand(m, k, generator=g, device="cuda") * 20 - 10).bfloat16()
+    x[0, :8] = torch.tensor([0.0, -0.0, 1e-3, -1e-3, 9.9, -9.9, 3.0, -3.0]).bfloat16()
+    eye = torch.eye(k, device="cuda").bfloat16()
+    out = torch.empty(m, k, device="cuda", dtype=torch.bfloat16)
+    _capi.linear(x, eye, None, _capi.EPI_BIAS_GELU, out)
+    exact = F.gelu(x.double(), approximate="none")
+    err = (out.double() - exact).abs()
+    tol = exact.abs() * 2.0**-8 + x.double().abs() * 2e-7
+    assert bool((err <= tol).all()), float((err - tol).max())
+    big = exact.abs() > 1e-3
+    mismatch = (out.float() != exact.bfloat16().float()) & big
+    assert mismatch.float().sum().item() <= 3e-3 * big.sum().item()  # measured: about 0.1%
+
+
 @pytest.mark.parametrize("m,n,k", GEMM_SHAPES)
 @pytest.mark.parametrize("zero", [False, True])
 def test_gemm_residual(m, n, k, zero):

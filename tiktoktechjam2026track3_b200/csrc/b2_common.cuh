@@ -530,8 +530,31 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
-// Exact (erf-based) GELU, the form torch.nn.functional.gelu(approximate="none") computes.
-__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f)); }
+__device__ __forceinline__ float fast_rcp(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float fast_exp2(float x);
+
+// Exact (erf-based) GELU, the form torch.nn.functional.gelu(approximate="none") computes:
+// 0.5 x (1 + erf(x / sqrt 2)). erf is evaluated with the rational-exponential formula 7.1.26 of
+// Abramowitz & Stegun, Handbook of Mathematical Functions (after Hastings):
+//   erf(z) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-z^2),  t = 1 / (1 + p z),  z >= 0,
+// whose absolute error is at most 1.5e-7 (the approximate reciprocal and exp2 add a few ulp),
+// far below the bf16 rounding the result goes through; odd symmetry gives z < 0.
+__device__ __forceinline__ float gelu_erf(float x) {
+  const float z = fabsf(x) * 0.70710678118654752440f;
+  const float t = fast_rcp(fmaf(0.3275911f, z, 1.0f));
+  float poly = fmaf(t, 1.061405429f, -1.453152027f);
+  poly = fmaf(t, poly, 1.421413741f);
+  poly = fmaf(t, poly, -0.284496736f);
+  poly = fmaf(t, poly, 0.254829592f);
+  poly *= t;
+  const float e = fast_exp2(z * (z * -1.44269504088896340736f));
+  const float erf_abs = fmaf(-poly, e, 1.0f);
+  return 0.5f * x * (1.0f + copysignf(erf_abs, x));
+}
 
 __device__ __forceinline__ float max3f(float a, float b, float c) {
   float r;

@@ -75,116 +75,101 @@ template <int EPI>
 __host__ __device__ constexpr bool is_mc_epi() {
   return EPI == kEpiMcResidual || EPI == kEpiMcResidualZero;
 }
-// The multicast epilogues transpose each warp's 32 x 32 fp32 chunk through shared memory so that
-// every multimem instruction covers whole 128-byte row segments (8 lanes x 16 B per row) instead
-// of 32 scattered 16-byte pieces: NVLink carries reductions as separate requests, and 16-byte
-// requests leave most of the link idle.
-constexpr int kMcStageBytes = (kGemmThreads / 32 - 2) * 32 * 32 * 4;
+
+// Epilogue staging: TMEM gives each lane one row of the accumulator, so a lane writing its own
+// row would make every warp-wide global access touch 32 different rows (32 memory transactions
+// of 16 bytes per instruction, and for the multicast epilogues 32 NVLink requests). Each epilogue
+// warp therefore passes its 32 x 32 fp32 chunk through 4 KB of shared memory and then works on
+// whole row segments: lane i handles columns 4(i % 8) .. +3 of rows i / 8, 4 + i / 8, ...
+constexpr int kEpiStageBytes = (kGemmThreads / 32 - 2) * 32 * 32 * 4;
 
 template <int BN, int EPI>
 struct GemmSmem {
-  static constexpr int kStages = (is_mc_epi<EPI>() && BN == 192) ? 4 : GemmCfg<BN>::kStages;
-  static constexpr int kEpiBytes = is_mc_epi<EPI>() ? kMcStageBytes : 0;
-  static constexpr int kBytes = kStages * GemmCfg<BN>::kStageBytes + 1024 + GemmCfg<BN>::kBarrierBytes + kEpiBytes;
+  static constexpr int kStages = BN == 192 ? 4 : GemmCfg<BN>::kStages;
+  static constexpr int kBytes =
+      kStages * GemmCfg<BN>::kStageBytes + 1024 + GemmCfg<BN>::kBarrierBytes + kEpiStageBytes;
   static_assert(kBytes <= 232448, "shared memory per CTA");
 };
 
-__device__ __forceinline__ void load_bias32(const __nv_bfloat16* bias, int col0, float (&b)[32]) {
-  if (bias == nullptr) {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) b[i] = 0.f;
-    return;
-  }
-  const uint4* src = reinterpret_cast<const uint4*>(bias + col0);
-#pragma unroll
-  for (int v = 0; v < 4; ++v) {
-    uint4 raw = __ldg(src + v);
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      b[v * 8 + 2 * k] = __low2float(h[k]);
-      b[v * 8 + 2 * k + 1] = __high2float(h[k]);
-    }
-  }
+__device__ __forceinline__ float4 load_bias4(const __nv_bfloat16* bias, int col) {
+  if (bias == nullptr) return make_float4(0.f, 0.f, 0.f, 0.f);
+  const uint2 raw = __ldg(reinterpret_cast<const uint2*>(bias + col));
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+  return make_float4(__low2float(h[0]), __high2float(h[0]), __low2float(h[1]), __high2float(h[1]));
 }
 
+// One warp's 32 rows x 32 columns (row0 = the warp's first row; lane i holds row row0 + i of
+// the accumulator in acc). The whole warp participates; rows >= M are skipped.
 template <int EPI>
-__device__ __forceinline__ void gemm_epilogue_chunk(const GemmParams& p, int row, int col0, const float (&acc)[32]) {
-  float b[32];
-  load_bias32(p.bias, col0, b);
-  if constexpr (EPI == kEpiBias || EPI == kEpiBiasGelu) {
-    uint32_t packed[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      float x0 = acc[2 * i] + b[2 * i];
-      float x1 = acc[2 * i + 1] + b[2 * i + 1];
-      if constexpr (EPI == kEpiBiasGelu) {
-        x0 = gelu_erf(bf16_round(x0));
-        x1 = gelu_erf(bf16_round(x1));
-      }
-      packed[i] = pack_bf16x2(x0, x1);
-    }
-    uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo + col0);
-#pragma unroll
-    for (int v = 0; v < 4; ++v)
-      dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
-  } else if constexpr (EPI == kEpiResidual || EPI == kEpiResidualZero) {
-    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + static_cast<int64_t>(row) * p.ldo + col0);
-    const bool keep = (p.row_mask == nullptr) || (p.row_mask[row] != 0);
-    if (keep) {
-#pragma unroll
-      for (int v = 0; v < 8; ++v) {
-        float4 r = dst[v];
-        r.x += acc[4 * v + 0] + b[4 * v + 0];
-        r.y += acc[4 * v + 1] + b[4 * v + 1];
-        r.z += acc[4 * v + 2] + b[4 * v + 2];
-        r.w += acc[4 * v + 3] + b[4 * v + 3];
-        dst[v] = r;
-      }
-    } else if constexpr (EPI == kEpiResidualZero) {
-#pragma unroll
-      for (int v = 0; v < 8; ++v) dst[v] = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-  } else {  // kEpiStoreF32
-    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + static_cast<int64_t>(row) * p.ldo + col0);
-#pragma unroll
-    for (int v = 0; v < 8; ++v)
-      dst[v] = make_float4(acc[4 * v] + b[4 * v], acc[4 * v + 1] + b[4 * v + 1], acc[4 * v + 2] + b[4 * v + 2],
-                           acc[4 * v + 3] + b[4 * v + 3]);
-  }
-}
-
-// Multicast epilogue of one warp's 32 rows x 32 columns (row0 = the warp's first row; lane i
-// holds row row0 + i in acc). Whole warp participates.
-template <int EPI>
-__device__ __forceinline__ void mc_epilogue_chunk(const GemmParams& p, int row0, int col0, const float (&acc)[32],
-                                                  float4* stage) {
+__device__ __forceinline__ void gemm_epilogue_chunk(const GemmParams& p, int row0, int col0, const float (&acc)[32],
+                                                    float4* stage) {
   const int lane = threadIdx.x & 31;
-  // Row `lane` as 8 float4 chunks, chunk index XOR-swizzled by the row so that both the stores
-  // (8 lanes = 8 rows, same chunk) and the loads below (8 lanes = 1 row, 8 chunks) touch all banks.
+  // Row `lane` as 8 float4 pieces, the piece index XOR-swizzled by the row, so that both these
+  // stores (8 lanes = 8 rows, same piece) and the loads below (8 lanes = one row, 8 pieces)
+  // spread over all 32 banks.
 #pragma unroll
   for (int c = 0; c < 8; ++c)
     stage[lane * 8 + (c ^ (lane & 7))] = make_float4(acc[4 * c], acc[4 * c + 1], acc[4 * c + 2], acc[4 * c + 3]);
   __syncwarp();
   const int q = lane & 7;
-  float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (p.bias != nullptr) {
-    const uint2 raw = *reinterpret_cast<const uint2*>(p.bias + col0 + 4 * q);
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
-    b = make_float4(__low2float(h[0]), __high2float(h[0]), __low2float(h[1]), __high2float(h[1]));
-  }
+  const int col = col0 + 4 * q;
+  const float4 b = load_bias4(p.bias, col);
+  // Gather the 8 row segments (and for the residual epilogues the residual itself) before any
+  // store, so that the loads are not ordered behind stores the compiler cannot tell apart.
+  float4 v[8];
+  bool live[8], keep[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int r = i * 4 + (lane >> 3);
     const int row = row0 + r;
-    const float4 v = stage[r * 8 + (q ^ (r & 7))];
-    if (row < p.M) {
-      float* dst = static_cast<float*>(p.out) + static_cast<int64_t>(row) * p.ldo + col0 + 4 * q;
-      const bool keep = (p.row_mask == nullptr) || (p.row_mask[row] != 0);
-      if (keep)
-        multimem_red_add_v4(dst, v.x + b.x, v.y + b.y, v.z + b.z, v.w + b.w);
-      else if constexpr (EPI == kEpiMcResidualZero)
-        multimem_st_v4(dst, 0.f, 0.f, 0.f, 0.f);
+    v[i] = stage[r * 8 + (q ^ (r & 7))];
+    v[i].x += b.x;
+    v[i].y += b.y;
+    v[i].z += b.z;
+    v[i].w += b.w;
+    live[i] = row < p.M;
+    keep[i] = live[i] && (p.row_mask == nullptr || p.row_mask[row] != 0);
+  }
+  if constexpr (EPI == kEpiResidual || EPI == kEpiResidualZero) {
+    float4 res[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int64_t off = static_cast<int64_t>(row0 + i * 4 + (lane >> 3)) * p.ldo + col;
+      if (keep[i]) res[i] = *reinterpret_cast<const float4*>(static_cast<const float*>(p.out) + off);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int64_t off = static_cast<int64_t>(row0 + i * 4 + (lane >> 3)) * p.ldo + col;
+      float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + off);
+      if (keep[i])
+        *dst = make_float4(res[i].x + v[i].x, res[i].y + v[i].y, res[i].z + v[i].z, res[i].w + v[i].w);
+      else if (EPI == kEpiResidualZero && live[i])
+        *dst = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (!live[i]) continue;
+      const int64_t off = static_cast<int64_t>(row0 + i * 4 + (lane >> 3)) * p.ldo + col;
+      if constexpr (EPI == kEpiBias || EPI == kEpiBiasGelu) {
+        float4 w = v[i];
+        if constexpr (EPI == kEpiBiasGelu) {
+          w.x = gelu_erf(bf16_round(w.x));
+          w.y = gelu_erf(bf16_round(w.y));
+          w.z = gelu_erf(bf16_round(w.z));
+          w.w = gelu_erf(bf16_round(w.w));
+        }
+        *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.out) + off) =
+            make_uint2(pack_bf16x2(w.x, w.y), pack_bf16x2(w.z, w.w));
+      } else if constexpr (EPI == kEpiStoreF32) {
+        *reinterpret_cast<float4*>(static_cast<float*>(p.out) + off) = v[i];
+      } else {  // multicast: every GPU's copy of the residual
+        float* dst = static_cast<float*>(p.out) + off;
+        if (keep[i])
+          multimem_red_add_v4(dst, v[i].x, v[i].y, v[i].z, v[i].w);
+        else if constexpr (EPI == kEpiMcResidualZero)
+          multimem_st_v4(dst, 0.f, 0.f, 0.f, 0.f);
+      }
     }
   }
   __syncwarp();
@@ -354,10 +339,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (col0 >= p.N) break;  // warp-uniform
         float v[32];
         tmem_load_32cols(t_row + c * 32, v);
-        if constexpr (is_mc_epi<EPI>())
-          mc_epilogue_chunk<EPI>(p, row - lane, col0, v, epi_stage);
-        else if (row < p.M)
-          gemm_epilogue_chunk<EPI>(p, row, col0, v);
+        gemm_epilogue_chunk<EPI>(p, row - lane, col0, v, epi_stage);
       }
       tc_fence_before_sync();
       mbar_arrive(&acc_empty[acc]);
@@ -393,7 +375,7 @@ struct Gemm2Cfg {
 };
 template <int BN, int EPI>
 constexpr int gemm2_smem_bytes() {
-  return Gemm2Cfg<BN>::kSmemBytes + (is_mc_epi<EPI>() ? kMcStageBytes : 0);
+  return Gemm2Cfg<BN>::kSmemBytes + kEpiStageBytes;
 }
 
 template <int BN, int EPI>
@@ -541,10 +523,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         if (col0 >= p.N) break;  // warp-uniform
         float v[32];
         tmem_load_32cols(t_row + c * 32, v);
-        if constexpr (is_mc_epi<EPI>())
-          mc_epilogue_chunk<EPI>(p, row - lane, col0, v, epi_stage);
-        else if (row < p.M)
-          gemm_epilogue_chunk<EPI>(p, row, col0, v);
+        gemm_epilogue_chunk<EPI>(p, row - lane, col0, v, epi_stage);
       }
       tc_fence_before_sync();
       mbar_arrive_cluster(acc ? acc_empty_leader1 : acc_empty_leader0);
