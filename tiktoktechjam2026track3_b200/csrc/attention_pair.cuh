@@ -12,27 +12,29 @@
 // alternates between the groups.
 //
 // CTA = (b, h, query-tile pair c), 11 warps:
-//   warp 0      TMA: Q tiles 2c, 2c+1 once; K_j and V_j (128 keys) into two independent 3-stage
+//   warp 0      TMA: Q tiles 2c, 2c+1 once; K_j and V_j (128 keys) into two independent 4-stage
 //               rings, each refilled as soon as its own slot frees (K never waits behind V).
 //   warps 1, 2  UMMA issuers, one per softmax group (warp 1 also allocates TMEM). tcgen05.mma
 //               issue blocks the issuing thread for about the instruction's execution time, so a
 //               single issuer serving both groups would make one group's P V delay the other's
 //               next S. Issuer t: S_t(j) = Q_t K_j^T into TMEM score buffer t, issued as soon as
-//               group t has S_t(j-1) in registers (s_free_t); O_t += P_t(j) [V_j | 1] (N = 64+16)
-//               accumulated in TMEM output buffer t once P_t(j) is published (p_full_t). A block of
-//               ones, addressed as the second 64-column block of the MN-major V operand (leading
-//               byte offset = distance from the V stage), makes columns 64..79 of O_t the running
-//               row sums of P. A K/V slot is refilled after both issuers released it (a group with
-//               fewer tiles releases the rest once each slot's previous use is done).
+//               group t has S_t(j-1) in registers (s_free_t); O_t += P_t(j) V_j accumulated in
+//               TMEM output buffer t once P_t(j) is published (p_full_t), with P_t read straight
+//               from tensor memory (A operand in TMEM) and V_j from shared memory. A K/V slot is
+//               refilled after both issuers released it (a group with fewer tiles releases the
+//               rest once each slot's previous use is done).
 //   warps 3..6  softmax group 0 (query tile 2c), warps 7..10 group 1 (tile 2c+1); warp % 4 is the
 //               TMEM lane quadrant = 32 query rows. Per KV tile a thread loads its row's 128 scores
-//               from TMEM, takes the row maximum, writes exp2(c*s - c*m) as bf16 into P_t
-//               (K-major, 128-byte swizzle, the layout the P V MMA reads) once P_t(j-1) V has been
-//               accumulated (o_full_t), and signals p_full_t. The reference maximum m
-//               of a row only moves when the tile maximum exceeds it by more than 2^8 in exp2
-//               units (probabilities up to 256 are exact enough in bf16/fp32); then, and only then,
-//               the warp waits for the previous accumulation and rescales its O_t rows (output and
-//               row-sum columns together) in TMEM. The final 1/l comes from the row-sum column.
+//               from TMEM, takes the row maximum, writes exp2(c*s - c*m) as bf16 pairs into P_t
+//               in tensor memory (tcgen05.st; lane = query row, column i = keys 2i, 2i+1) once
+//               P_t(j-1) V has been accumulated (o_full_t), adds the fp32 values to its running
+//               row sum, and signals p_full_t. The reference maximum m of a row only moves when
+//               the tile maximum exceeds it by more than 2^8 in exp2 units (probabilities up to
+//               256 are exact enough in bf16/fp32); then, and only then, the warp waits for the
+//               previous accumulation and rescales its O_t rows in TMEM (and its row sum).
+//
+// Tensor memory: S_0, S_1 (128 columns each), P_0, P_1 (64), O_0, O_1 (64) = 512 columns.
+// Shared memory traffic per tile is Q, K (S MMA) and V (P V MMA) only; P never leaves TMEM.
 #pragma once
 #include "b2_common.cuh"
 
@@ -44,19 +46,17 @@ struct AttnPairCfg {
   static constexpr int kQBytes = kBoxBytes;            // one 128 x 64 query tile
   static constexpr int kKBytes = kBoxBytes;
   static constexpr int kVBytes = kBoxBytes;
-  static constexpr int kPBytes = 2 * kBoxBytes;        // 128 rows x 128 keys bf16
-  static constexpr int kStages = 3;
+  static constexpr int kStages = 4;
   static constexpr int kOffQ = 0;                                   // [2]
   static constexpr int kOffK = kOffQ + 2 * kQBytes;                 // [kStages]
   static constexpr int kOffV = kOffK + kStages * kKBytes;           // [kStages]
-  static constexpr int kOffOnes = kOffV + kStages * kVBytes;        // one 128 x 64 block of bf16 ones
-  static constexpr int kOffP = kOffOnes + kBoxBytes;                // [2 groups]
-  static constexpr int kOffBar = kOffP + 2 * kPBytes;
+  static constexpr int kOffBar = kOffV + kStages * kVBytes;
   static constexpr int kSmemBytes = kOffBar + 256 + 1024;
+  // Tensor memory (512 columns x 128 lanes of 32 bits): scores, probabilities, outputs.
   static constexpr int kTmemCols = 512;
-  static constexpr int kSCol = 0;      // S_t at t * 128
-  static constexpr int kOCol = 256;    // O_t at 256 + t * 128 (80 columns used)
-  static constexpr int kON = 80;       // P V MMA N: 64 output columns + 16 row-sum columns
+  static constexpr int kSCol = 0;      // S_t: 128 fp32 columns at t * 128
+  static constexpr int kPCol = 256;    // P_t: 128 bf16 keys packed in 64 columns at 256 + t * 64
+  static constexpr int kOCol = 384;    // O_t: 64 fp32 columns at 384 + t * 64
 };
 
 // Row maximum of 32 values as a balanced tree of 3-input maxima (short dependency chains).
@@ -81,19 +81,18 @@ __global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
   uint8_t* s_q = smem + Cfg::kOffQ;
   uint8_t* s_k = smem + Cfg::kOffK;
   uint8_t* s_v = smem + Cfg::kOffV;
-  uint8_t* s_p = smem + Cfg::kOffP;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;    // [kStages]
-  uint64_t* k_empty = bars + 4;   // [kStages]
-  uint64_t* v_full = bars + 7;    // [kStages]
-  uint64_t* v_empty = bars + 10;  // [kStages]
-  uint64_t* s_full = bars + 13;   // [2 groups]
-  uint64_t* p_full = bars + 15;   // [2 groups]
-  uint64_t* o_full = bars + 17;   // [2 groups]
-  uint64_t* s_free = bars + 19;   // [2 groups]
-  uint64_t* drain = bars + 21;    // [2 issuers]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 23);
+  uint64_t* k_full = q_full + 1;               // [kStages]
+  uint64_t* k_empty = k_full + Cfg::kStages;   // [kStages]
+  uint64_t* v_full = k_empty + Cfg::kStages;   // [kStages]
+  uint64_t* v_empty = v_full + Cfg::kStages;   // [kStages]
+  uint64_t* s_full = v_empty + Cfg::kStages;   // [2 groups]
+  uint64_t* p_full = s_full + 2;               // [2 groups]
+  uint64_t* o_full = p_full + 2;               // [2 groups]
+  uint64_t* s_free = o_full + 2;               // [2 groups]
+  uint64_t* drain = s_free + 2;                // [2 issuers]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -140,12 +139,6 @@ __global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
     tmem_relinquish();
   }
-  {
-    uint4* ones = reinterpret_cast<uint4*>(smem + Cfg::kOffOnes);
-    for (int i = threadIdx.x; i < Cfg::kBoxBytes / 16; i += Cfg::kThreads)
-      ones[i] = make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
-  }
-  fence_proxy_async_smem();
   tc_fence_before_sync();
   __syncthreads();
   tc_fence_after_sync();
@@ -216,10 +209,11 @@ __global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
     const int t = warp - 1;
     if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc_bf16_f32(128, 128, 0, 0);
-      constexpr uint32_t idesc_o = make_idesc_bf16_f32(128, Cfg::kON, 0, 1);
+      constexpr uint32_t idesc_o = make_idesc_bf16_f32(128, HD, 0, 1);
       const uint32_t q_addr = smem_u32(s_q) + t * Cfg::kQBytes;
       const uint32_t d_s = tmem_base + Cfg::kSCol + t * 128;
-      const uint32_t d_o = tmem_base + Cfg::kOCol + t * 128;
+      const uint32_t d_o = tmem_base + Cfg::kOCol + t * HD;
+      const uint32_t a_p = tmem_base + Cfg::kPCol + t * 64;
       const int n = n_kv[t];
       auto issue_s = [&](int j) {
         const uint32_t k_addr = smem_u32(s_k + (j % Cfg::kStages) * Cfg::kKBytes);
@@ -231,14 +225,14 @@ __global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
         umma_commit(&k_empty[j % Cfg::kStages]);
       };
       auto issue_o = [&](int j) {
-        const uint32_t p_addr = smem_u32(s_p + t * Cfg::kPBytes);
         const int vst = j % Cfg::kStages;
         const uint32_t v_addr = smem_u32(s_v + vst * Cfg::kVBytes);
-        const uint32_t ones_lbo = static_cast<uint32_t>(Cfg::kOffOnes - Cfg::kOffV - vst * Cfg::kVBytes);
+        // A = P_t from tensor memory (16 keys = 8 packed columns per step), B = V_j (MN-major: one
+        // 64-wide swizzle atom of head dims, 16 keys = 2048 bytes per step).
 #pragma unroll
         for (int kk = 0; kk < 128 / 16; ++kk)
-          umma_bf16_ss(d_o, make_sdesc_sw128(p_addr + (kk >> 2) * Cfg::kBoxBytes + (kk & 3) * 32, 16, 1024),
-                       make_sdesc_sw128(v_addr + kk * 2048, ones_lbo, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          umma_bf16_ts(d_o, a_p + kk * 8, make_sdesc_sw128(v_addr + kk * 2048, 16, 1024), idesc_o,
+                       (j > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&o_full[t]);
         umma_commit(&v_empty[vst]);
       };
@@ -302,13 +296,17 @@ __global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
     const int n = grp == 0 ? n_kv[0] : n_kv[1];
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
     const uint32_t t_s = t_lane + Cfg::kSCol + grp * 128;
-    const uint32_t t_o = t_lane + Cfg::kOCol + grp * 128;
-    uint8_t* prow = s_p + grp * Cfg::kPBytes + (r >> 3) * 1024 + (r & 7) * 128;
+    const uint32_t t_o = t_lane + Cfg::kOCol + grp * HD;
+    const uint32_t t_p = t_lane + Cfg::kPCol + grp * 64;
     const float c = p.scale_log2;
     const int limit = p.causal ? min(kv_len, query + 1) : kv_len;
     constexpr float kRescaleThreshold = 8.0f;  // exp2 units: rescale only when m grows by > 2^8
+    // Exponentials moved to the FMA pipe (bit k: pair k of every 4). Measured on B200 at this
+    // kernel's register budget: 0 is fastest (moving a quarter or a half costs spills).
+    constexpr int kPolyPairs = 0x0;            // pair 3 of every 4 on the FMA pipe: a quarter of the exponentials
 
     float m_ref = 0.f;  // reference maximum (raw score units) used in exp2(c * (s - m_ref))
+    float l_sum = 0.f;  // running sum of exp2(c * (s - m_ref)) over the row's keys (fp32)
     bool alive = true;
 
     // Ping-pong of the exponential phase between the groups: group g runs its exp2 loop only
@@ -365,20 +363,34 @@ __global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
 #pragma unroll
           for (int k = 0; k < 128; ++k) v[k] = (k < n_valid) ? v[k] : -INFINITY;
         }
-        const float neg_mc = -m_ref * c;
-        // probabilities -> P_t: row r, keys 8q..8q+7 = 16-byte chunk (q % 8) of atom q / 8
+        const uint64_t c2 = splat2(c);
+        const uint64_t neg_mc2 = splat2(-m_ref * c);
+        // probabilities -> P_t in tensor memory: row r = lane r, keys 2i, 2i+1 packed in column i.
+        // Pairs selected by kPolyPairs take 2^x on the FMA pipe (exp2_poly_x2), the others on the
+        // exponential unit, so that both pipes share the 16384 exponentials of a tile.
+        float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          uint32_t w[4];
+        for (int g = 0; g < 4; ++g) {
+          uint32_t w[16];
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float e0 = fast_exp2(fmaf(v[8 * q + 2 * k], c, neg_mc));
-            const float e1 = fast_exp2(fmaf(v[8 * q + 2 * k + 1], c, neg_mc));
+          for (int k = 0; k < 16; ++k) {
+            float x0 = v[32 * g + 2 * k], x1 = v[32 * g + 2 * k + 1];
+            fma2_inplace(x0, x1, c2, neg_mc2);
+            float e0, e1;
+            if ((kPolyPairs >> (k & 3)) & 1) {
+              exp2_poly_x2(x0, x1, e0, e1);
+            } else {
+              e0 = fast_exp2(x0);
+              e1 = fast_exp2(x1);
+            }
+            sum0 += e0;
+            sum1 += e1;
             w[k] = pack_bf16x2(e0, e1);
           }
-          *reinterpret_cast<uint4*>(prow + (q >> 3) * Cfg::kBoxBytes + (((q & 7) ^ (r & 7)) << 4)) =
-              make_uint4(w[0], w[1], w[2], w[3]);
+          tmem_store_16cols_async(t_p + 16 * g, w);
         }
+        l_sum = l_sum * alpha + (sum0 + sum1);
+        tmem_wait_st();
       }
       if (grp == 0)
         named_barrier_arrive(2, 256);
@@ -391,7 +403,7 @@ __global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
           // of tile j-1 has landed (waited above) and P_t(j) V is not issued before p_full_t.
           // Warp-uniform: the TMEM loads and stores are warp-collective.
 #pragma unroll 1
-          for (int cc = 0; cc < 3; ++cc) {
+          for (int cc = 0; cc < HD / 32; ++cc) {
             float o[32];
             tmem_load_32cols(t_o + cc * 32, o);
 #pragma unroll
@@ -399,7 +411,6 @@ __global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
             tmem_store_32cols(t_o + cc * 32, o);
           }
         }
-        fence_proxy_async_smem();
         tc_fence_before_sync();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[grp]);
@@ -409,8 +420,7 @@ __global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
     if (n > 0) {
       softmax_wait(&o_full[grp], (n - 1) & 1, 30, alive, abort_flag);
       tc_fence_after_sync();
-      const float l = tmem_load_1col(t_o + HD);
-      const float inv = l > 0.f ? 1.0f / l : 0.f;
+      const float inv = l_sum > 0.f ? 1.0f / l_sum : 0.f;
       float o[64];
       tmem_load_32cols(t_o, o);
       tmem_load_32cols(t_o + 32, o + 32);

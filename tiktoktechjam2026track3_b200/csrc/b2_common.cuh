@@ -333,6 +333,18 @@ __device__ __forceinline__ void umma_bf16_ss(uint32_t d_tmem, uint64_t a_desc, u
       : "memory");
 }
 
+// D (+)= A * B^T with A read from tensor memory (128 lanes = M rows; K packed two bf16 per 32-bit
+// column, so a K = 16 step spans 8 columns) and B from shared memory.
+__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // 2-SM UMMA issued by the pair's leader: D (M=256 across both CTAs' TMEM) (+)= A * B^T, where each
 // CTA supplies half of A's rows and half of B's rows from its own shared memory at the addresses
 // the descriptors give.
@@ -442,6 +454,17 @@ __device__ __forceinline__ void tmem_load_128cols(uint32_t taddr, float* v) {
 
 // Stores 32 fp32 values into 32 consecutive columns of this thread's TMEM lane and waits for the
 // store to complete (tcgen05.st is .sync.aligned like tcgen05.ld).
+// 16 columns of this warp's 32 TMEM lanes; completion is awaited separately (tmem_wait_st).
+__device__ __forceinline__ void tmem_store_16cols_async(uint32_t taddr, const uint32_t* w) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(taddr),
+      "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7]), "r"(w[8]),
+      "r"(w[9]), "r"(w[10]), "r"(w[11]), "r"(w[12]), "r"(w[13]), "r"(w[14]), "r"(w[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 __device__ __forceinline__ void tmem_store_32cols(uint32_t taddr, const float* v) {
   __syncwarp();
   asm volatile(
@@ -580,6 +603,33 @@ __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x for two values on the FMA pipe instead of the exponential unit (MUFU, 16/clk/SM, which
+// is what bounds a head_dim-64 softmax). Range reduction: n = rint(x) by the 1.5 * 2^23
+// round-to-integer addition, f = x - n in [-1/2, 1/2] (both exact); 2^f by a cubic whose
+// coefficients were fitted for minimax relative error over that interval (iteratively
+// reweighted least squares): max relative error 7.5e-5, against bf16's half-ulp of 2^-9. The
+// exponent n is added to the cubic's exponent field with one integer multiply-add (the low 9
+// bits of the rounded float hold n). x is clamped below at -126 so the field cannot wrap
+// (-inf gives a denormal-or-zero result, never NaN); x above 127 is outside the contract.
+__device__ __forceinline__ void exp2_poly_x2(float x0, float x1, float& e0, float& e1) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  x0 = fmaxf(x0, -126.0f);
+  x1 = fmaxf(x1, -126.0f);
+  uint64_t x, t, r, f, p;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(x0), "f"(x1));
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(t) : "l"(x), "l"(splat2(kRound)));
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(t), "l"(splat2(kRound)));
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(f) : "l"(x), "l"(r));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(p) : "l"(f), "l"(splat2(0.05517132f)), "l"(splat2(0.24261054f)));
+  asm("fma.rn.f32x2 %0, %0, %1, %2;" : "+l"(p) : "l"(f), "l"(splat2(0.69326099f)));
+  asm("fma.rn.f32x2 %0, %0, %1, %2;" : "+l"(p) : "l"(f), "l"(splat2(0.99992811f)));
+  float p0, p1, t0, t1;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(p0), "=f"(p1) : "l"(p));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(t0), "=f"(t1) : "l"(t));
+  e0 = __int_as_float(__float_as_int(t0) * (1 << 23) + __float_as_int(p0));
+  e1 = __int_as_float(__float_as_int(t1) * (1 << 23) + __float_as_int(p1));
 }
 
 }  // namespace b2
