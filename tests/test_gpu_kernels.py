@@ -201,6 +201,9 @@ ATTN_CASES = [
     (2, 2048, 4, 64, True, None),
     (1, 640, 2, 64, False, None),
     (2, 512, 12, 64, False, [256, 511]),
+    (2, 300, 2, 128, False, [300, 129]),
+    (1, 4096, 2, 128, True, None),
+    (1, 384, 1, 128, False, None),
 ]
 
 

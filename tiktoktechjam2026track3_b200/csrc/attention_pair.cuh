@@ -1,15 +1,16 @@
-// Flash attention forward for head_dim 64 with two query tiles per CTA (the paths of
+// Flash attention forward (head_dim 64 and 128) with two query tiles per CTA (the paths of
 // BaselineSelfAttention.forward, transformer_benchmark/models.py:55-75; masks as in
 // attention.cuh).
 //
-// Why a separate kernel for head_dim 64: a 128x128 score tile costs the tensor core 2 x 128x128x64
-// MACs (S = Q K^T and O = P V, ~512 clocks) but costs the exponential unit 16384 ex2 (~1024 clocks
-// at 16/clk/SM), so the softmax, not the MMA, sets the pace. With one query tile per CTA every
-// softmax warp waits through the same latency phases (TMEM loads, row maximum, wait for the next
-// S) at the same time and the exponential unit idles. Here each CTA owns query tiles 2c and 2c+1
-// with two independent 4-warp softmax groups; each thread owns one whole query row (no exchange
-// between warps), so one group's exponentials run while the other group waits, and the tensor core
-// alternates between the groups.
+// Why two query tiles per CTA: a 128x128 score tile costs the tensor core 2 x 128x128xhd MACs
+// (S = Q K^T and O = P V: ~512 clocks at hd 64, ~1024 at hd 128) and the exponential unit 16384
+// ex2 (~1024 clocks at 16/clk/SM), so at head_dim 64 the softmax, not the MMA, sets the pace and
+// at 128 the two are even. With one query tile per CTA every softmax warp waits through the same
+// latency phases (TMEM loads, row maximum, wait for the next S) at the same time and the
+// exponential unit idles. Here each CTA owns query tiles 2c and 2c+1 with two independent 4-warp
+// softmax groups; each thread owns one whole query row (no exchange between warps), so one
+// group's exponentials run while the other group waits, and the tensor core alternates between
+// the groups.
 //
 // CTA = (b, h, query-tile pair c), 11 warps:
 //   warp 0      TMA: Q tiles 2c, 2c+1 once; K_j and V_j (128 keys) into two independent 4-stage
@@ -40,23 +41,33 @@
 
 namespace b2 {
 
+template <int HD>
 struct AttnPairCfg {
   static constexpr int kThreads = 352;
-  static constexpr int kBoxBytes = 128 * 128;          // 128 rows x 64 bf16 columns
-  static constexpr int kQBytes = kBoxBytes;            // one 128 x 64 query tile
-  static constexpr int kKBytes = kBoxBytes;
-  static constexpr int kVBytes = kBoxBytes;
-  static constexpr int kStages = 4;
+  static constexpr int kBoxBytes = 128 * 128;          // 128 rows x 64 bf16 columns (one TMA box)
+  static constexpr int kBoxes = HD / 64;               // boxes per 128-row tile
+  static constexpr int kQBytes = kBoxes * kBoxBytes;   // one 128 x HD query tile
+  static constexpr int kKBytes = kQBytes;
+  static constexpr int kVBytes = kQBytes;
+  static constexpr int kStages = HD == 64 ? 4 : 2;
   static constexpr int kOffQ = 0;                                   // [2]
   static constexpr int kOffK = kOffQ + 2 * kQBytes;                 // [kStages]
   static constexpr int kOffV = kOffK + kStages * kKBytes;           // [kStages]
   static constexpr int kOffBar = kOffV + kStages * kVBytes;
   static constexpr int kSmemBytes = kOffBar + 256 + 1024;
   // Tensor memory (512 columns x 128 lanes of 32 bits): scores, probabilities, outputs.
+  //   head_dim 64:  S_t at t * 128, P_t (128 bf16 keys packed in 64 columns) at 256 + t * 64,
+  //                 O_t (64 columns) at 384 + t * 64.
+  //   head_dim 128: S_t at t * 128 with P_t written over its first 64 columns (the scores are
+  //                 in registers by then), O_t (128 columns) at 256 + t * 128. S_t(j+1) is issued
+  //                 only after P_t(j) V has completed.
+  static constexpr bool kPAliasS = HD == 128;
   static constexpr int kTmemCols = 512;
-  static constexpr int kSCol = 0;      // S_t: 128 fp32 columns at t * 128
-  static constexpr int kPCol = 256;    // P_t: 128 bf16 keys packed in 64 columns at 256 + t * 64
-  static constexpr int kOCol = 384;    // O_t: 64 fp32 columns at 384 + t * 64
+  static constexpr int kSCol = 0;
+  static constexpr int kPCol = kPAliasS ? 0 : 256;
+  static constexpr int kPStride = kPAliasS ? 128 : 64;
+  static constexpr int kOCol = kPAliasS ? 256 : 384;
+  static_assert(kSmemBytes <= 232448, "shared memory per CTA");
 };
 
 // Row maximum of 32 values as a balanced tree of 3-input maxima (short dependency chains).
@@ -72,10 +83,10 @@ __device__ __forceinline__ float max32(const float* v) {
   return fmaxf(max3f(b0, b1, b2), b3);
 }
 
-__global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
+template <int HD>
+__global__ void __launch_bounds__(AttnPairCfg<HD>::kThreads, 1)
     attention_pair_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnParams p) {
-  using Cfg = AttnPairCfg;
-  constexpr int HD = 64;
+  using Cfg = AttnPairCfg<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* s_q = smem + Cfg::kOffQ;
@@ -153,8 +164,11 @@ __global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
       const int kc = p.k_col + h * HD;
       const int vc = p.v_col + h * HD;
       mbar_arrive_expect_tx(q_full, 2 * Cfg::kQBytes);
-      tma_load_2d(s_q, &tm_qkv, q_full, qc, q_row0);
-      tma_load_2d(s_q + Cfg::kQBytes, &tm_qkv, q_full, qc, q_row0 + 128);
+#pragma unroll
+      for (int c = 0; c < Cfg::kBoxes; ++c) {
+        tma_load_2d(s_q + c * Cfg::kBoxBytes, &tm_qkv, q_full, qc + 64 * c, q_row0);
+        tma_load_2d(s_q + Cfg::kQBytes + c * Cfg::kBoxBytes, &tm_qkv, q_full, qc + 64 * c, q_row0 + 128);
+      }
       // K and V rings refill independently (polling both), so a K tile never waits for a V slot.
       int k_next = 0, v_next = 0;
       bool ok = true;
@@ -166,7 +180,10 @@ __global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
             mbar_test_wait(&k_empty[k_next % Cfg::kStages], ((k_next / Cfg::kStages) & 1) ^ 1u)) {
           const int st = k_next % Cfg::kStages;
           mbar_arrive_expect_tx(&k_full[st], Cfg::kKBytes);
-          tma_load_2d(s_k + st * Cfg::kKBytes, &tm_qkv, &k_full[st], kc, row_base + k_next * 128);
+#pragma unroll
+          for (int c = 0; c < Cfg::kBoxes; ++c)
+            tma_load_2d(s_k + st * Cfg::kKBytes + c * Cfg::kBoxBytes, &tm_qkv, &k_full[st], kc + 64 * c,
+                        row_base + k_next * 128);
           ++k_next;
           progress = true;
         }
@@ -174,7 +191,10 @@ __global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
             mbar_test_wait(&v_empty[v_next % Cfg::kStages], ((v_next / Cfg::kStages) & 1) ^ 1u)) {
           const int st = v_next % Cfg::kStages;
           mbar_arrive_expect_tx(&v_full[st], Cfg::kVBytes);
-          tma_load_2d(s_v + st * Cfg::kVBytes, &tm_qkv, &v_full[st], vc, row_base + v_next * 128);
+#pragma unroll
+          for (int c = 0; c < Cfg::kBoxes; ++c)
+            tma_load_2d(s_v + st * Cfg::kVBytes + c * Cfg::kBoxBytes, &tm_qkv, &v_full[st], vc + 64 * c,
+                        row_base + v_next * 128);
           ++v_next;
           progress = true;
         }
@@ -213,39 +233,54 @@ __global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
       const uint32_t q_addr = smem_u32(s_q) + t * Cfg::kQBytes;
       const uint32_t d_s = tmem_base + Cfg::kSCol + t * 128;
       const uint32_t d_o = tmem_base + Cfg::kOCol + t * HD;
-      const uint32_t a_p = tmem_base + Cfg::kPCol + t * 64;
+      const uint32_t a_p = tmem_base + Cfg::kPCol + t * Cfg::kPStride;
       const int n = n_kv[t];
       auto issue_s = [&](int j) {
         const uint32_t k_addr = smem_u32(s_k + (j % Cfg::kStages) * Cfg::kKBytes);
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk)
-          umma_bf16_ss(d_s, make_sdesc_sw128(q_addr + kk * 32, 16, 1024),
-                       make_sdesc_sw128(k_addr + kk * 32, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * Cfg::kBoxBytes + (kk & 3) * 32;
+          umma_bf16_ss(d_s, make_sdesc_sw128(q_addr + off, 16, 1024), make_sdesc_sw128(k_addr + off, 16, 1024),
+                       idesc_s, kk > 0 ? 1u : 0u);
+        }
         umma_commit(&s_full[t]);
         umma_commit(&k_empty[j % Cfg::kStages]);
       };
       auto issue_o = [&](int j) {
         const int vst = j % Cfg::kStages;
         const uint32_t v_addr = smem_u32(s_v + vst * Cfg::kVBytes);
-        // A = P_t from tensor memory (16 keys = 8 packed columns per step), B = V_j (MN-major: one
-        // 64-wide swizzle atom of head dims, 16 keys = 2048 bytes per step).
+        // A = P_t from tensor memory (16 keys = 8 packed columns per step), B = V_j (MN-major:
+        // 64-wide swizzle atoms of head dims, one box apart; 16 keys = 2048 bytes per step).
 #pragma unroll
         for (int kk = 0; kk < 128 / 16; ++kk)
-          umma_bf16_ts(d_o, a_p + kk * 8, make_sdesc_sw128(v_addr + kk * 2048, 16, 1024), idesc_o,
+          umma_bf16_ts(d_o, a_p + kk * 8, make_sdesc_sw128(v_addr + kk * 2048, Cfg::kBoxBytes, 1024), idesc_o,
                        (j > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&o_full[t]);
         umma_commit(&v_empty[vst]);
       };
       bool ok = n == 0 || mbar_wait(q_full, 0, abort_flag, kKernelAttention, 23);
       for (int j = 0; j < n && ok; ++j) {
-        // S_t(j): K_j loaded and (j > 0) S_t(j-1) taken by the softmax group.
+        // S_t(j): K_j loaded and (j > 0) S_t(j-1) taken by the softmax group; with P_t stored
+        // over S_t, also P_t(j-1) V complete.
         if (!mbar_wait(&k_full[j % Cfg::kStages], (j / Cfg::kStages) & 1, abort_flag, kKernelAttention, 24) ||
-            (j > 0 && !mbar_wait(&s_free[t], (j - 1) & 1, abort_flag, kKernelAttention, 25))) {
+            (j > 0 && !mbar_wait(&s_free[t], (j - 1) & 1, abort_flag, kKernelAttention, 25)) ||
+            (Cfg::kPAliasS && j > 0 && !mbar_wait(&o_full[t], (j - 1) & 1, abort_flag, kKernelAttention, 33))) {
           ok = false;
           break;
         }
         tc_fence_after_sync();
         issue_s(j);
+        if (Cfg::kPAliasS) {
+          // O_t += P_t(j) V_j as soon as published: S_t(j + 1) waits for it anyway.
+          if (!mbar_wait(&p_full[t], j & 1, abort_flag, kKernelAttention, 26) ||
+              !mbar_wait(&v_full[j % Cfg::kStages], (j / Cfg::kStages) & 1, abort_flag, kKernelAttention, 27)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after_sync();
+          issue_o(j);
+          continue;
+        }
         // O_t += P_t(j-1) V_{j-1} once published (issued after S_t(j) so the scores come first).
         if (j > 0) {
           if (!mbar_wait(&p_full[t], (j - 1) & 1, abort_flag, kKernelAttention, 26) ||
@@ -258,7 +293,7 @@ __global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
           issue_o(j - 1);
         }
       }
-      if (ok && n > 0) {
+      if (ok && n > 0 && !Cfg::kPAliasS) {
         if (!mbar_wait(&p_full[t], (n - 1) & 1, abort_flag, kKernelAttention, 26) ||
             !mbar_wait(&v_full[(n - 1) % Cfg::kStages], ((n - 1) / Cfg::kStages) & 1, abort_flag, kKernelAttention,
                        27)) {
@@ -297,7 +332,7 @@ __global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
     const uint32_t t_s = t_lane + Cfg::kSCol + grp * 128;
     const uint32_t t_o = t_lane + Cfg::kOCol + grp * HD;
-    const uint32_t t_p = t_lane + Cfg::kPCol + grp * 64;
+    const uint32_t t_p = t_lane + Cfg::kPCol + grp * Cfg::kPStride;
     const float c = p.scale_log2;
     const int limit = p.causal ? min(kv_len, query + 1) : kv_len;
     constexpr float kRescaleThreshold = 8.0f;  // exp2 units: rescale only when m grows by > 2^8
@@ -421,17 +456,19 @@ __global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
       softmax_wait(&o_full[grp], (n - 1) & 1, 30, alive, abort_flag);
       tc_fence_after_sync();
       const float inv = l_sum > 0.f ? 1.0f / l_sum : 0.f;
-      float o[64];
-      tmem_load_32cols(t_o, o);
-      tmem_load_32cols(t_o + 32, o + 32);
-      if (query < p.S) {
-        uint4* dst = reinterpret_cast<uint4*>(p.ctx + static_cast<int64_t>(row_base + query) * p.ld_ctx + h * HD);
+      uint4* dst = reinterpret_cast<uint4*>(p.ctx + static_cast<int64_t>(row_base + query) * p.ld_ctx + h * HD);
 #pragma unroll
-        for (int k = 0; k < HD / 8; ++k)
-          dst[k] = make_uint4(pack_bf16x2(o[8 * k] * inv, o[8 * k + 1] * inv),
-                              pack_bf16x2(o[8 * k + 2] * inv, o[8 * k + 3] * inv),
-                              pack_bf16x2(o[8 * k + 4] * inv, o[8 * k + 5] * inv),
-                              pack_bf16x2(o[8 * k + 6] * inv, o[8 * k + 7] * inv));
+      for (int cc = 0; cc < HD / 32; ++cc) {
+        float o[32];
+        tmem_load_32cols(t_o + 32 * cc, o);
+        if (query < p.S) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            dst[4 * cc + k] = make_uint4(pack_bf16x2(o[8 * k] * inv, o[8 * k + 1] * inv),
+                                         pack_bf16x2(o[8 * k + 2] * inv, o[8 * k + 3] * inv),
+                                         pack_bf16x2(o[8 * k + 4] * inv, o[8 * k + 5] * inv),
+                                         pack_bf16x2(o[8 * k + 6] * inv, o[8 * k + 7] * inv));
+        }
       }
     }
   }
@@ -443,18 +480,20 @@ __global__ void __launch_bounds__(AttnPairCfg::kThreads, 1)
   }
 }
 
+template <int HD>
 static cudaError_t launch_attention_pair(const CUtensorMap& tm, const AttnParams& p, cudaStream_t stream) {
+  using Cfg = AttnPairCfg<HD>;
   static std::once_flag once[64];
   int dev = 0;
   cudaGetDevice(&dev);
   cudaError_t attr_err = cudaSuccess;
   std::call_once(once[dev & 63], [&] {
-    attr_err = cudaFuncSetAttribute(attention_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    AttnPairCfg::kSmemBytes);
+    attr_err = cudaFuncSetAttribute(attention_pair_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    Cfg::kSmemBytes);
   });
   if (attr_err != cudaSuccess) return attr_err;
   dim3 grid(p.B * p.H, (p.n_q_tiles + 1) / 2);
-  return launch_pdl(attention_pair_kernel, grid, dim3(AttnPairCfg::kThreads), AttnPairCfg::kSmemBytes, stream, tm, p);
+  return launch_pdl(attention_pair_kernel<HD>, grid, dim3(Cfg::kThreads), Cfg::kSmemBytes, stream, tm, p);
 }
 
 }  // namespace b2
