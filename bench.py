@@ -54,6 +54,11 @@ UNIT = "tokens/s"
 PER_GPU_BATCH = {"c1": 2, "c2": 8, "c3": 16, "c4": 1, "c5": 4}
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 L2_FLUSH_BYTES = 256 << 20
+LONG_STEP_MS = 50.0
+# DRAM bytes (read + write) per launch of the dominant kernel class, averaged over the class's
+# launches in one forward, from an ncu capture of this bench (profiles/launches_bench_c2.md):
+# key = (workload, tensor-parallel ranks, kernel class).
+DRAM_BYTES_PER_LAUNCH = {("c2", 1, "gemm_tc_kernel"): 19168888.0}
 
 
 def parse_args(argv=None):
@@ -116,55 +121,87 @@ def layernorm_bytes(cfg: TransformerConfig) -> float:
 
 # ----------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons of one GPU while the timed region runs."""
+    """Samples SM clock, power and clock-event reasons of one GPU while the timed region runs.
 
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
-    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+    Reads NVML (read-only queries) from a background thread every 2 ms, so that even a timed
+    region of a few milliseconds gets samples; falls back to `nvidia-smi -lms 200` without NVML.
+    """
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown"}
 
     def __init__(self, device: torch.device):
         props = torch.cuda.get_device_properties(device)
         self.bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
-        self.proc = None
+        self.samples: list = []
+        self._stop = None
+        self._thread = None
+        self._proc = None
+        self.source = "nvml"
+
+    def _nvml_loop(self, nv, handle):
+        while not self._stop.is_set():
+            try:
+                self.samples.append((nv.nvmlDeviceGetClockInfo(handle, nv.NVML_CLOCK_SM),
+                                     nv.nvmlDeviceGetMaxClockInfo(handle, nv.NVML_CLOCK_SM),
+                                     nv.nvmlDeviceGetPowerUsage(handle) / 1000.0,
+                                     nv.nvmlDeviceGetCurrentClocksEventReasons(handle)))
+            except Exception:  # noqa: BLE001 - a failed query only loses one sample
+                pass
+            self._stop.wait(0.002)
 
     def start(self):
+        import threading
+
+        self.samples = []
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.bus}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+            import pynvml as nv
+
+            nv.nvmlInit()
+            handle = nv.nvmlDeviceGetHandleByPciBusId(self.bus)
+            self._stop = threading.Event()
+            self._thread = threading.Thread(target=self._nvml_loop, args=(nv, handle), daemon=True)
+            self._thread.start()
+            return
+        except Exception:  # noqa: BLE001 - NVML missing: use nvidia-smi instead
+            self.source = "nvidia-smi"
+        fields = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.sw_power_cap,"
+                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                  "clocks_event_reasons.hw_thermal_slowdown")
+        try:
+            self._proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.bus}", f"--query-gpu={fields}", "--format=csv,noheader,nounits",
                  "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
-            self.proc = None
+            self._proc = None
 
     def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "note": "nvidia-smi unavailable"}
-        self.proc.terminate()
-        try:
-            out, _ = self.proc.communicate(timeout=10)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-            out, _ = self.proc.communicate()
-        sm, sm_max, power, reasons = [], [], [], set()
-        for line in out.strip().splitlines():
-            parts = [s.strip() for s in line.split(",")]
-            if len(parts) < 7:
-                continue
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
+        elif self._proc is not None:
+            self._proc.terminate()
             try:
-                sm.append(float(parts[0]))
-                sm_max.append(float(parts[1]))
-                power.append(float(parts[2]))
-            except ValueError:
-                continue
-            for name, flag in zip(self.NAMES, parts[3:7]):
-                if flag.lower().startswith("active"):
-                    reasons.add(name)
+                out, _ = self._proc.communicate(timeout=10)
+            except subprocess.TimeoutExpired:
+                self._proc.kill()
+                out, _ = self._proc.communicate()
+            for line in out.strip().splitlines():
+                parts = [x.strip() for x in line.split(",")]
+                try:
+                    bits = sum(bit for bit, flag in zip(self.REASONS, parts[3:7]) if flag.lower().startswith("active"))
+                    self.samples.append((float(parts[0]), float(parts[1]), float(parts[2]), bits))
+                except (ValueError, IndexError):
+                    continue
+        else:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "source": "unavailable"}
+        reasons = sorted({name for _, _, _, bits in self.samples for bit, name in self.REASONS.items() if bits & bit})
         return {
-            "sm_mhz": statistics.median(sm) if sm else None,
-            "sm_max_mhz": max(sm_max) if sm_max else None,
-            "power_w_max": max(power) if power else None,
-            "reasons": sorted(reasons),
-            "samples": len(sm),
+            "sm_mhz": statistics.median(x[0] for x in self.samples) if self.samples else None,
+            "sm_max_mhz": max(x[1] for x in self.samples) if self.samples else None,
+            "power_w_max": max(x[2] for x in self.samples) if self.samples else None,
+            "reasons": reasons,
+            "samples": len(self.samples),
+            "source": self.source,
         }
 
 
@@ -382,10 +419,15 @@ def main() -> None:
         gemm_total /= world
         attn /= world
     peaks, peak_src = measured_peaks()
+    # A kernel inside a long step runs at the power-capped clock: compare it with the sustained
+    # GEMM figure; short steps run at boost clock: the burst figure.
+    long_step = ms_per_step > LONG_STEP_MS
+    tensor_peak = peaks["bf16_tflops_sustained"] if long_step else peaks["bf16_tflops"]
+    tensor_peak_name = "bf16 sustained" if long_step else "bf16 burst"
     classes = {
         "gemm_tc_kernel": {"ms": gemm_ms, "work": gemm_total, "bound": "tensor",
                            "launches": sum(v for k, v in kind_n.items() if k.startswith("gemm")) // reps},
-        "attention_tc_kernel": {"ms": kind_ms.get("attention", 0.0), "work": attn, "bound": "tensor",
+        "attention_pair_kernel": {"ms": kind_ms.get("attention", 0.0), "work": attn, "bound": "tensor",
                                 "launches": kind_n.get("attention", 0) // reps},
         "layernorm_vec_kernel": {"ms": kind_ms.get("layernorm", 0.0), "work": layernorm_bytes(cfg), "bound": "hbm",
                                  "launches": kind_n.get("layernorm", 0) // reps},
@@ -396,7 +438,7 @@ def main() -> None:
             continue
         if c["bound"] == "tensor":
             achieved = c["work"] / (c["ms"] / 1e3) / 1e12
-            peak = peaks["bf16_tflops"]
+            peak = tensor_peak
             unit = "TFLOP/s"
         else:
             achieved = c["work"] / (c["ms"] / 1e3) / 1e9
@@ -410,15 +452,15 @@ def main() -> None:
         "kernel": dominant,
         "bound": classes[dominant]["bound"],
         "achieved": dk["achieved"],
-        "peak": peaks["bf16_tflops"] if classes[dominant]["bound"] == "tensor" else peaks["hbm_gbs"],
-        "peak_source": f"{peak_src} ({'bf16 burst' if classes[dominant]['bound'] == 'tensor' else 'HBM copy'})",
+        "peak": tensor_peak if classes[dominant]["bound"] == "tensor" else peaks["hbm_gbs"],
+        "peak_source": f"{peak_src} ({tensor_peak_name if classes[dominant]['bound'] == 'tensor' else 'HBM copy'})",
         "unit": dk["unit"],
         "frac": dk["frac"],
-        "traffic": None,
+        "traffic": DRAM_BYTES_PER_LAUNCH.get((args.workload, world if tensor_parallel else 1, dominant)),
         "work_per_launch": classes[dominant]["work"] / max(1, classes[dominant]["launches"]),
     }
     total_flops = gemm_total + attn  # per rank
-    mfu = total_flops / (ms_per_step / 1e3) / 1e12 / peaks["bf16_tflops"]
+    mfu = total_flops / (ms_per_step / 1e3) / 1e12 / tensor_peak
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
