@@ -12,7 +12,7 @@
 // group's exponentials run while the other group waits, and the tensor core alternates between
 // the groups.
 //
-// CTA = (b, h, query-tile pair c), 11 warps:
+// CTA = (b, h, query-tile pair c), 12 warps at head_dim 64, 11 at head_dim 128:
 //   warp 0      TMA: Q tiles 2c, 2c+1 once; K_j and V_j (128 keys) into two independent 4-stage
 //               rings, each refilled as soon as its own slot frees (K never waits behind V).
 //   warps 1, 2  UMMA issuers, one per softmax group (warp 1 also allocates TMEM). tcgen05.mma
@@ -24,7 +24,9 @@
 //               from tensor memory (A operand in TMEM) and V_j from shared memory. A K/V slot is
 //               refilled after both issuers released it (a group with fewer tiles releases the
 //               rest once each slot's previous use is done).
-//   warps 3..6  softmax group 0 (query tile 2c), warps 7..10 group 1 (tile 2c+1); warp % 4 is the
+//   warp 3      (head_dim 64) spare, keeping the control warpgroup whole for the register split.
+//   next 8      softmax group 0 (query tile 2c: warps 3..6 at head_dim 128, 4..7 at 64), then
+//               group 1 (tile 2c+1); warp % 4 is the
 //               TMEM lane quadrant = 32 query rows. Per KV tile a thread loads its row's 128 scores
 //               from TMEM, takes the row maximum, writes exp2(c*s - c*m) as bf16 pairs into P_t
 //               in tensor memory (tcgen05.st; lane = query row, column i = keys 2i, 2i+1) once
@@ -43,7 +45,19 @@ namespace b2 {
 
 template <int HD>
 struct AttnPairCfg {
-  static constexpr int kThreads = 352;
+  // head_dim 64 (exponential-bound): 3 warpgroups — control (TMA, two UMMA issuers, a spare
+  // warp), softmax group 0, group 1 — with the launch's 384 x 168 registers split as control 72,
+  // softmax 216 (128 x 72 + 256 x 216 = 64512), so a softmax thread has room to run a quarter of
+  // its exponentials on the FMA pipe (kPolyPairs) next to its 128 scores.
+  // head_dim 128 (MMA and exponentials even): 11 warps, uniform 168 registers, all exponentials
+  // on the exponential unit. Measured on B200: each choice is the faster one for its head_dim.
+  static constexpr bool kSplitRegs = HD == 64;
+  static constexpr int kThreads = kSplitRegs ? 384 : 352;
+  static constexpr int kSoftmaxWarp0 = kSplitRegs ? 4 : 3;
+  static constexpr int kLaunchRegs = 168;
+  static constexpr int kCtrlRegs = 72;
+  static constexpr int kSoftmaxRegs = 216;
+  static constexpr int kPolyPairs = kSplitRegs ? 0x8 : 0x0;  // bit k: pair k of every 4 on the FMA pipe
   static constexpr int kBoxBytes = 128 * 128;          // 128 rows x 64 bf16 columns (one TMA box)
   static constexpr int kBoxes = HD / 64;               // boxes per 128-row tile
   static constexpr int kQBytes = kBoxes * kBoxBytes;   // one 128 x HD query tile
@@ -156,8 +170,12 @@ __global__ void __launch_bounds__(AttnPairCfg<HD>::kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   pdl_wait_previous_grid();
   pdl_allow_next_grid();
+  static_assert(!Cfg::kSplitRegs || 128 * Cfg::kCtrlRegs + 256 * Cfg::kSoftmaxRegs <= Cfg::kThreads * Cfg::kLaunchRegs,
+                "register split");
 
-  if (warp == 0) {
+  if (warp < Cfg::kSoftmaxWarp0) {
+   if constexpr (Cfg::kSplitRegs) regs_dec<Cfg::kCtrlRegs>();
+   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       const int qc = p.q_col + h * HD;
@@ -321,9 +339,11 @@ __global__ void __launch_bounds__(AttnPairCfg<HD>::kThreads, 1)
       while (!mbar_try_wait(&drain[t], 0) && global_timer_ns() - t0 < kWaitTimeoutNs) {
       }
     }
+   }
   } else {
+    if constexpr (Cfg::kSplitRegs) regs_inc<Cfg::kSoftmaxRegs>();
     // ---------------- softmax groups ----------------
-    const int grp = (warp - 3) >> 2;
+    const int grp = (warp - Cfg::kSoftmaxWarp0) >> 2;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     const int qt = 2 * pair + grp;
@@ -336,9 +356,7 @@ __global__ void __launch_bounds__(AttnPairCfg<HD>::kThreads, 1)
     const float c = p.scale_log2;
     const int limit = p.causal ? min(kv_len, query + 1) : kv_len;
     constexpr float kRescaleThreshold = 8.0f;  // exp2 units: rescale only when m grows by > 2^8
-    // Exponentials moved to the FMA pipe (bit k: pair k of every 4). Measured on B200 at this
-    // kernel's register budget: 0 is fastest (moving a quarter or a half costs spills).
-    constexpr int kPolyPairs = 0x0;            // pair 3 of every 4 on the FMA pipe: a quarter of the exponentials
+    constexpr int kPolyPairs = Cfg::kPolyPairs;
 
     float m_ref = 0.f;  // reference maximum (raw score units) used in exp2(c * (s - m_ref))
     float l_sum = 0.f;  // running sum of exp2(c * (s - m_ref)) over the row's keys (fp32)
