@@ -141,7 +141,7 @@ def attention_core(
                 scores = scores.masked_fill(hidden[None], float("-inf"))
             if key_mask is not None:
                 scores = scores.masked_fill(~key_mask[b, None, None, :k_stop], float("-inf"))
-            probs = torch.softmax(scores, dim=-1)
+            probs = torch.softmax(scores.float(), dim=-1).to(scores.dtype)  # fp32 softmax (models.py:69)
             out[b, :, r0:r1] = torch.matmul(probs, vb[:, :k_stop])
     return out
 
@@ -179,10 +179,15 @@ def forward(
     x: torch.Tensor,
     valid_token_mask: Optional[torch.Tensor] = None,
     query_chunk: int = 1024,
+    dtype: torch.dtype = torch.float32,
 ) -> torch.Tensor:
-    """BaselineTransformer.forward (models.py:909-919) in fp32 on x's device."""
+    """BaselineTransformer.forward (models.py:909-919) on x's device, in fp32 by default.
+
+    With dtype=torch.bfloat16 (and a bf16 state) every op runs in bf16 with the softmax in fp32,
+    as the reference's baseline module does on the GPU in the harness's bf16 mode.
+    """
     _, _, _, num_heads, _, num_layers, causal = _config_fields(config)
-    x = x.to(torch.float32)
+    x = x.to(dtype)
     for i in range(num_layers):
         p = f"layers.{i}"
         x = x + self_attention(_layer_norm(x, state, f"{p}.norm1"), state, f"{p}.attention", num_heads,

@@ -54,8 +54,11 @@ def test_linear_rejects_null_and_bad_shapes(lib):
 
 def test_attention_rejects_unsupported_head_dim(lib):
     p = ctypes.c_void_p(16)
-    assert lib.b2_attention_fwd(p, 96, 0, 32, 64, 1, 8, 1, 32, None, 1, 0.1, p, 32, None) == 2
+    assert lib.b2_attention_fwd(p, 144, 0, 48, 96, 1, 8, 1, 48, None, 1, 0.1, p, 48, None) == 2
     assert b"head_dim" in lib.b2_last_error()
+    # CUDA-core head dims need 8-element column alignment, tensor-core ones 64
+    assert lib.b2_attention_fwd(p, 96, 0, 36, 64, 1, 8, 1, 32, None, 1, 0.1, p, 32, None) == 2
+    assert b"multiples of 8" in lib.b2_last_error()
     assert lib.b2_attention_fwd(p, 192, 0, 32, 128, 1, 8, 1, 64, None, 1, 0.1, p, 64, None) == 2
     assert lib.b2_attention_fwd(None, 192, 0, 64, 128, 1, 8, 1, 64, None, 1, 0.1, p, 64, None) == 1
 

@@ -204,6 +204,14 @@ ATTN_CASES = [
     (2, 300, 2, 128, False, [300, 129]),
     (1, 4096, 2, 128, True, None),
     (1, 384, 1, 128, False, None),
+    # CUDA-core kernel (head dims of the reference's official case matrix)
+    (2, 128, 4, 32, True, None),
+    (3, 200, 4, 8, False, [200, 77, 1]),
+    (2, 128, 4, 256, True, None),
+    (1, 1024, 4, 32, True, None),
+    (4, 32, 4, 32, True, None),
+    (2, 130, 16, 8, True, [130, 65]),
+    (2, 96, 2, 16, False, None),
 ]
 
 

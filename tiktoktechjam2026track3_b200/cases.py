@@ -120,3 +120,23 @@ def generate_random_case(
     mask = positions < lengths[:, None]
     x = x.masked_fill(~mask[..., None], 0)
     return x, mask
+
+
+# The reference's official case matrix (competition appendix 3.7; transformer_benchmark/cases.py:
+# 42-57): case ids are one-based positions in this tuple, as the reference numbers them.
+OFFICIAL_TEST_CASES: Tuple[TransformerConfig, ...] = (
+    TransformerConfig(64, 128, 128, 4, 128, 4, True),
+    TransformerConfig(1, 128, 128, 4, 128, 4, True),
+    TransformerConfig(4, 128, 128, 4, 128, 4, True),
+    TransformerConfig(16, 128, 128, 4, 128, 4, True),
+    TransformerConfig(128, 128, 128, 4, 128, 4, True),
+    TransformerConfig(10000, 128, 128, 4, 128, 4, True),
+    TransformerConfig(64, 128, 32, 4, 32, 4, True),
+    TransformerConfig(64, 128, 1024, 4, 1024, 4, True),
+    TransformerConfig(64, 128, 128, 1, 128, 4, True),
+    TransformerConfig(64, 128, 128, 2, 128, 4, True),
+    TransformerConfig(64, 128, 128, 16, 128, 4, True),
+    TransformerConfig(64, 32, 128, 4, 128, 4, True),
+    TransformerConfig(64, 1024, 128, 4, 128, 4, True),
+    TransformerConfig(32, 100000, 1024, 16, 1024, 2, True),
+)

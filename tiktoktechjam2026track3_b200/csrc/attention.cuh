@@ -1,6 +1,6 @@
-// Flash-style multi-head self-attention forward on tcgen05 tensor cores: the shared parameters,
-// the host entry point, and the softmax wait helper. The kernel itself (one template for
-// head_dim 64 and 128) is in attention_pair.cuh.
+// Flash-style multi-head self-attention forward: the shared parameters, the host entry point,
+// and the softmax wait helper. The tcgen05 kernel for head_dim 64 and 128 is in
+// attention_pair.cuh; head dims 8, 16, 32 and 256 run on CUDA cores (attention_simt.cuh).
 //
 // Computes, per batch b, head h and query q (BaselineSelfAttention.forward,
 // transformer_benchmark/models.py:55-75):
@@ -50,13 +50,13 @@ cudaError_t make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner
 template <int HD>
 static cudaError_t launch_attention_pair(const CUtensorMap& tm, const AttnParams& p, cudaStream_t stream);
 
+template <int HD>
+static cudaError_t launch_attention_simt(const __nv_bfloat16* qkv, int64_t ld_qkv, const AttnParams& p,
+                                         cudaStream_t stream);
+
 cudaError_t launch_attention(const __nv_bfloat16* qkv, int64_t ld_qkv, int64_t q_col, int64_t k_col, int64_t v_col,
                              int64_t B, int64_t S, int64_t H, int64_t hd, const int32_t* kv_len, int causal,
                              float scale, __nv_bfloat16* ctx, int64_t ld_ctx, cudaStream_t stream) {
-  CUtensorMap tm;
-  cudaError_t e = make_tmap_bf16_2d(&tm, qkv, static_cast<uint64_t>(ld_qkv), static_cast<uint64_t>(B * S),
-                                    static_cast<uint64_t>(ld_qkv) * 2, 64, 128);
-  if (e != cudaSuccess) return e;
   AttnParams p;
   p.ctx = ctx;
   p.ld_ctx = ld_ctx;
@@ -70,9 +70,25 @@ cudaError_t launch_attention(const __nv_bfloat16* qkv, int64_t ld_qkv, int64_t q
   p.causal = causal;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.n_q_tiles = static_cast<int>((S + 127) / 128);
+  switch (hd) {
+    case 8:
+      return launch_attention_simt<8>(qkv, ld_qkv, p, stream);
+    case 16:
+      return launch_attention_simt<16>(qkv, ld_qkv, p, stream);
+    case 32:
+      return launch_attention_simt<32>(qkv, ld_qkv, p, stream);
+    case 256:
+      return launch_attention_simt<256>(qkv, ld_qkv, p, stream);
+    default:
+      break;
+  }
+  if (hd != 64 && hd != 128) return cudaErrorInvalidValue;
+  CUtensorMap tm;
+  cudaError_t e = make_tmap_bf16_2d(&tm, qkv, static_cast<uint64_t>(ld_qkv), static_cast<uint64_t>(B * S),
+                                    static_cast<uint64_t>(ld_qkv) * 2, 64, 128);
+  if (e != cudaSuccess) return e;
   if (hd == 64) return launch_attention_pair<64>(tm, p, stream);
-  if (hd == 128) return launch_attention_pair<128>(tm, p, stream);
-  return cudaErrorInvalidValue;
+  return launch_attention_pair<128>(tm, p, stream);
 }
 
 }  // namespace b2

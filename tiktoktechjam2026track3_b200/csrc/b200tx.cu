@@ -20,6 +20,7 @@
 #include "gemm.cuh"
 #include "attention.cuh"
 #include "attention_pair.cuh"
+#include "attention_simt.cuh"
 #include "peer.cuh"
 
 #define B2_API extern "C" __attribute__((visibility("default")))
@@ -163,10 +164,13 @@ B2_API int b2_attention_fwd(const void* qkv, int64_t ld_qkv, int64_t q_col, int6
                             int causal, float scale, void* ctx, int64_t ld_ctx, void* stream) {
   if (qkv == nullptr || ctx == nullptr) return fail(1, "b2_attention_fwd: null pointer argument");
   if (batch < 0 || seq_len < 0 || num_heads <= 0) return fail(1, "b2_attention_fwd: invalid shape");
-  if (head_dim != 64 && head_dim != 128) return fail(2, "b2_attention_fwd: head_dim=%lld not supported (64, 128)",
-                                                     (long long)head_dim);
-  if (q_col % 64 || k_col % 64 || v_col % 64 || q_col < 0 || k_col < 0 || v_col < 0)
-    return fail(2, "b2_attention_fwd: q/k/v column offsets must be non-negative multiples of 64");
+  const bool tensor_core = head_dim == 64 || head_dim == 128;
+  if (!tensor_core && head_dim != 8 && head_dim != 16 && head_dim != 32 && head_dim != 256)
+    return fail(2, "b2_attention_fwd: head_dim=%lld not supported (8, 16, 32, 64, 128, 256)", (long long)head_dim);
+  const int64_t col_align = tensor_core ? 64 : 8;
+  if (q_col % col_align || k_col % col_align || v_col % col_align || q_col < 0 || k_col < 0 || v_col < 0)
+    return fail(2, "b2_attention_fwd: q/k/v column offsets must be non-negative multiples of %lld",
+                (long long)col_align);
   const int64_t width = num_heads * head_dim;
   if (q_col + width > ld_qkv || k_col + width > ld_qkv || v_col + width > ld_qkv)
     return fail(1, "b2_attention_fwd: q/k/v columns exceed ld_qkv");

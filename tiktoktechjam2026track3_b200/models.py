@@ -36,6 +36,10 @@ import torch.nn as nn
 from . import _capi
 from .cases import TransformerConfig, config_from
 
+# 64 and 128 run on the tcgen05 attention kernel; 8, 16, 32 and 256 (the reference's official
+# case matrix) on the CUDA-core one.
+SUPPORTED_HEAD_DIMS = (8, 16, 32, 64, 128, 256)
+
 
 class SelfAttention(nn.Module):
     """Parameter holder with BaselineSelfAttention's names (models.py:20-33)."""
@@ -207,8 +211,8 @@ class UserOptimizedTransformer(nn.Module):
             raise RuntimeError("UserOptimizedTransformer runs on CUDA (sm_100a) only; x is on the CPU")
         if x.dtype != torch.bfloat16:
             raise RuntimeError(f"UserOptimizedTransformer computes in bfloat16; got x.dtype={x.dtype}")
-        if cfg.head_dim not in (64, 128):
-            raise NotImplementedError(f"head_dim {cfg.head_dim} is not supported (64 or 128)")
+        if cfg.head_dim not in SUPPORTED_HEAD_DIMS:
+            raise NotImplementedError(f"head_dim {cfg.head_dim} is not supported {SUPPORTED_HEAD_DIMS}")
         batch, seq_len, d_model = x.shape
         if valid_token_mask is not None and valid_token_mask.device != x.device:
             raise ValueError("valid_token_mask must be on x's device")
