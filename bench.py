@@ -68,8 +68,9 @@ def parse_args(argv=None):
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--workload", default="c2", choices=sorted(BASELINE_CONFIGS))
     p.add_argument("--impl", default="ours", choices=("ours", "reference"))
-    p.add_argument("--collective", default="auto", choices=("auto", "multimem", "nccl"),
-                   help="tensor-parallel reduction: fused into the GEMMs over NVLS multicast, or NCCL all-reduce")
+    p.add_argument("--collective", default="auto", choices=("auto", "rs", "nccl"),
+                   help="tensor-parallel reduction: reduce-scatter in the GEMMs + all-gather in the LayerNorm over "
+                        "NVLink (rs), or NCCL all-reduce")
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
     p.add_argument("--cpu-seconds", type=float, default=15.0, help="target CPU time of the CPU baseline sample")
     return p.parse_args(argv)
@@ -491,10 +492,11 @@ def main() -> None:
                 "layers": cfg.num_layers,
                 "causal": cfg.causal,
                 "padding_ratio": pad,
-                "parallelism": (f"tp{world} (heads / FFN columns; " + (
-                    "out_proj / ffn_out GEMM epilogues add their partial tiles into every GPU's fp32 residual "
-                    "with multimem.red over NVSwitch, 4 flag barriers per block)" if model.collective == "multimem"
-                    else "2 NCCL all-reduces of the fp32 [T, D] partial per block)"))
+                "parallelism": (f"tp{world} (heads / FFN columns; " + {
+                    "rs": "out_proj / ffn_out GEMM epilogues add each row into its owner's fp32 residual over "
+                          "NVLink (reduce-scatter), owners' LayerNorm rows stored into every GPU's buffer (all-gather), "
+                          "4 flag barriers per block)",
+                    "nccl": "2 NCCL all-reduces of the fp32 [T, D] partial per block)"}[model.collective])
                 if tensor_parallel else f"dp{world} (batch shards, no collective)",
                 "l2": "flushed (256 MiB write) before every timed step",
                 "launches": (f"eager launches ({model.collective})" if tensor_parallel else

@@ -41,12 +41,6 @@ extern "C" {
 #define B2_EPI_RESIDUAL 2       /* out f32 (in place) = mask ? out + acc + bias : out    */
 #define B2_EPI_RESIDUAL_ZERO 3  /* out f32 (in place) = mask ? out + acc + bias : 0      */
 #define B2_EPI_STORE_F32 4      /* out f32 = acc (+ bias if non-null)                     */
-/* Tensor parallel with the all-reduce fused into the GEMM: `out` is the NVLS multicast address of a
- * replicated fp32 residual [m, ldo] (e.g. torch symmetric memory's multicast_ptr); each rank's
- * partial acc (+ bias, passed on one rank only) is added into every GPU's copy with multimem.red
- * as tiles finish. The caller orders other reads/writes of the residual with cross-GPU barriers. */
-#define B2_EPI_MC_RESIDUAL 5       /* every copy: kept rows += acc + bias                   */
-#define B2_EPI_MC_RESIDUAL_ZERO 6  /* every copy: kept rows += acc + bias, masked rows = 0  */
 
 /* b2_linear_fwd tile_n flag: the 2-SM variant (a CTA pair computes 256-row tiles with
  * tcgen05.mma.cta_group::2), combined with an N tile of 192 or 256. */
@@ -119,8 +113,36 @@ int b2_attention_fwd(const void* qkv, int64_t ld_qkv, int64_t q_col, int64_t k_c
                      float scale, void* ctx, int64_t ld_ctx, void* stream);
 
 /*
+ * Tensor-parallel reduce-scatter fused into a residual GEMM: out = A W^T (+ bias) is added with
+ * fp32 atomics (system scope) into the residual copy of the rank that owns each row — rank
+ * r / rows_per_rank — so after every rank's call each owner holds its rows' full sum. No
+ * counterpart in the reference (one GPU); replaces out_proj / ffn_out + NCCL all-reduce
+ * (models.py:76, 734) under head / FFN-column tensor parallelism.
+ *   peer_resid  host array of `world` device pointers: every rank's fp32 residual [m, ldo] as
+ *               mapped into this process (peer memory over NVLink); the caller's is peer_resid[rank]
+ *   bias        [n] bf16, passed on one rank only
+ *   zero_masked_rows  rows with row_mask 0 are set to 0 by their owner (ffn_out), else kept
+ * The caller orders the owners' reads of the residual against the adds (b2_peer_barrier).
+ */
+int b2_linear_rs_fwd(const void* a, const void* w, const void* bias, int64_t m, int64_t n, int64_t k,
+                     int zero_masked_rows, void* const* peer_resid, int world, int rank, int64_t rows_per_rank,
+                     int64_t ldo, const uint8_t* row_mask, int tile_n, void* stream);
+
+/*
+ * LayerNorm of fp32 rows (x [rows, d_model]) written as bf16 into the same rows of every
+ * tensor-parallel rank's buffer: the all-gather of a LayerNorm whose rows are split over the ranks
+ * (nn.LayerNorm, models.py:721, 723, 907; no counterpart for the gather). y_ranks is a host array
+ * of `world` device pointers (each rank's destination for the first row, as mapped into this
+ * process — the caller's own buffer and NVLink peer buffers). row_mask 0 rows are written as 0.
+ * d_model = 256 * {1, 2, 3, 4, 8, 16}. The caller orders the readers with b2_peer_barrier.
+ */
+int b2_layernorm_gather_fwd(const float* x, const void* gamma, const void* beta, float eps, void* const* y_ranks,
+                            int world, const uint8_t* row_mask, int64_t rows, int64_t d_model, void* stream);
+
+/*
  * Cross-GPU barrier for tensor-parallel runs whose all-reduce is fused into the GEMM epilogues
- * (B2_EPI_MC_RESIDUAL*). No counterpart in the reference, which runs on one GPU; in this build
+ * (b2_linear_rs_fwd) and the all-gather into the LayerNorm (b2_layernorm_gather_fwd). No
+ * counterpart in the reference, which runs on one GPU; in this build
  * it takes the place of the synchronisation an NCCL all-reduce gives.
  *   pads    host array of `world` device pointers: every rank's flag pad (4 x 8 uint32, zeroed
  *           before first use) as mapped into this process (e.g. symmetric memory buffer_ptrs)

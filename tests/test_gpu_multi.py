@@ -1,8 +1,8 @@
 """Multi-GPU plans on B200s (needs 2+ GPUs; skipped otherwise): one process per GPU over NCCL.
 
 * tensor parallel (heads/FFN columns) agrees with the single-GPU model within the parity gate
-  (reduction order differs, so not bitwise), both with the reduction fused into the GEMM
-  epilogues over NVLS multicast (where the GPUs support it) and with the NCCL all-reduce;
+  (reduction order differs, so not bitwise), both with the reduce-scatter fused into the GEMM
+  epilogues and the all-gather into the LayerNorm ("rs") and with the NCCL all-reduce;
 * a batch shard on rank r is bit-identical to the same sequences of the single-GPU run.
 """
 
@@ -18,7 +18,7 @@ import torch.multiprocessing as mp
 from oracle import reference_fp32 as oracle
 from tiktoktechjam2026track3_b200 import UserOptimizedTransformer, baseline_gate
 from tiktoktechjam2026track3_b200.cases import TransformerConfig
-from tiktoktechjam2026track3_b200.sharding import TensorParallelTransformer, batch_shard, multicast_supported
+from tiktoktechjam2026track3_b200.sharding import TensorParallelTransformer, batch_shard
 
 pytestmark = pytest.mark.gpu
 
@@ -41,7 +41,7 @@ def _worker(rank, world, port, cfg, pad, q):
         model = UserOptimizedTransformer(cfg)
         model.load_state_dict(state, strict=True)
         model = model.to(device=dev, dtype=torch.bfloat16).eval()
-        collectives = ["nccl"] + (["multimem"] if multicast_supported(dev) else [])
+        collectives = ["nccl", "rs"]
         with torch.inference_mode():
             single = model(xb, mask)
             b0, b1 = batch_shard(cfg.batch_size, world, rank)

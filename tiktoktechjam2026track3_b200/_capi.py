@@ -26,8 +26,6 @@ EPI_BIAS_GELU = 1
 EPI_RESIDUAL = 2
 EPI_RESIDUAL_ZERO = 3
 EPI_STORE_F32 = 4
-EPI_MC_RESIDUAL = 5
-EPI_MC_RESIDUAL_ZERO = 6
 TILE_PAIR = 0x10000
 
 # Every symbol include/b200tx.h declares, with its ctypes signature.
@@ -54,6 +52,14 @@ SIGNATURES = {
         [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, ctypes.c_int, ctypes.c_float, _vp, _i64, _vp],
     ),
     "b2_peer_barrier": (ctypes.c_int, [ctypes.POINTER(_vp), ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
+    "b2_linear_rs_fwd": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _i64, _i64, _i64, ctypes.c_int, ctypes.POINTER(_vp), ctypes.c_int, ctypes.c_int, _i64, _i64,
+         _vp, ctypes.c_int, _vp],
+    ),
+    "b2_layernorm_gather_fwd": (
+        ctypes.c_int, [_vp, _vp, _vp, ctypes.c_float, ctypes.POINTER(_vp), ctypes.c_int, _vp, _i64, _i64, _vp],
+    ),
 }
 
 _lock = threading.Lock()
@@ -188,17 +194,11 @@ def linear(
     w: torch.Tensor,
     bias: Optional[torch.Tensor],
     epilogue: int,
-    out: Optional[torch.Tensor],
+    out: torch.Tensor,
     row_mask: Optional[torch.Tensor] = None,
     tile_n: int = 0,
-    out_ptr: Optional[int] = None,
-    out_ld: Optional[int] = None,
 ) -> None:
-    """out = epilogue(a @ w.T + bias) (see b2_linear_fwd).
-
-    For the multicast epilogues (EPI_MC_*) pass `out_ptr` (an NVLS multicast address of an fp32
-    [m, out_ld] buffer) and `out_ld` instead of `out`.
-    """
+    """out = epilogue(a @ w.T + bias) (see b2_linear_fwd)."""
     _require(a, torch.bfloat16, "a")
     _require(w, torch.bfloat16, "w")
     m, k = a.shape[0] if a.dim() == 2 else a.numel() // a.shape[-1], a.shape[-1]
@@ -207,16 +207,11 @@ def linear(
         raise ValueError(f"w has shape {tuple(w.shape)}, expected [n, {k}]")
     if bias is not None:
         _require(bias, torch.bfloat16, "bias")
-    if epilogue in (EPI_MC_RESIDUAL, EPI_MC_RESIDUAL_ZERO):
-        if out is not None or out_ptr is None or out_ld is None:
-            raise ValueError("multicast epilogues take out_ptr and out_ld (and no out tensor)")
-        dst, ldo = int(out_ptr), int(out_ld)
-    else:
-        out_dtype = torch.bfloat16 if epilogue in (EPI_BIAS, EPI_BIAS_GELU) else torch.float32
-        _require(out, out_dtype, "out")
-        if out.numel() < m * n:
-            raise ValueError("out is too small")
-        dst, ldo = out.data_ptr(), out.shape[-1]
+    out_dtype = torch.bfloat16 if epilogue in (EPI_BIAS, EPI_BIAS_GELU) else torch.float32
+    _require(out, out_dtype, "out")
+    if out.numel() < m * n:
+        raise ValueError("out is too small")
+    dst, ldo = out.data_ptr(), out.shape[-1]
     if row_mask is not None:
         _require(row_mask, torch.uint8, "row_mask")
     status = load_library().b2_linear_fwd(
@@ -265,3 +260,48 @@ def peer_barrier(pads, rank: int, channel: int, device: torch.device) -> None:
     arr = (_vp * len(pads))(*[int(p) for p in pads])
     status = load_library().b2_peer_barrier(arr, len(pads), int(rank), int(channel), _stream_ptr(device))
     _check(status, "b2_peer_barrier")
+
+
+def linear_rs(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], zero_masked_rows: bool, peer_resid,
+              rank: int, rows_per_rank: int, ldo: int, row_mask: Optional[torch.Tensor] = None, tile_n: int = 0) -> None:
+    """Residual GEMM whose rows are added into their owner rank's residual (see b2_linear_rs_fwd).
+
+    `peer_resid` lists every rank's residual base address (ints) as mapped into this process.
+    """
+    _require(a, torch.bfloat16, "a")
+    _require(w, torch.bfloat16, "w")
+    m, k = a.shape
+    n = w.shape[0]
+    if w.shape[1] != k:
+        raise ValueError("a and w disagree on K")
+    if bias is not None:
+        _require(bias, torch.bfloat16, "bias")
+    if row_mask is not None:
+        _require(row_mask, torch.uint8, "row_mask")
+    arr = (_vp * len(peer_resid))(*[int(x) for x in peer_resid])
+    status = load_library().b2_linear_rs_fwd(
+        _ptr(a), _ptr(w), _ptr(bias), m, n, k, 1 if zero_masked_rows else 0, arr, len(peer_resid), int(rank),
+        int(rows_per_rank), int(ldo), _ptr(row_mask), int(tile_n), _stream_ptr(a.device),
+    )
+    _check(status, "b2_linear_rs_fwd")
+
+
+def layernorm_gather(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float, y_ranks,
+                     row_mask: Optional[torch.Tensor] = None) -> None:
+    """LayerNorm of fp32 rows x written as bf16 into every rank's buffer (see b2_layernorm_gather_fwd).
+
+    `y_ranks` lists each rank's destination address (ints) for x's first row.
+    """
+    _require(x, torch.float32, "x")
+    _require(gamma, torch.bfloat16, "gamma")
+    _require(beta, torch.bfloat16, "beta")
+    if row_mask is not None:
+        _require(row_mask, torch.uint8, "row_mask")
+    d_model = x.shape[-1]
+    rows = x.numel() // d_model
+    arr = (_vp * len(y_ranks))(*[int(p) for p in y_ranks])
+    status = load_library().b2_layernorm_gather_fwd(
+        _ptr(x), _ptr(gamma), _ptr(beta), float(eps), arr, len(y_ranks), _ptr(row_mask), rows, d_model,
+        _stream_ptr(x.device),
+    )
+    _check(status, "b2_layernorm_gather_fwd")

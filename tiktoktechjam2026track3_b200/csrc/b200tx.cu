@@ -135,7 +135,9 @@ B2_API int b2_linear_fwd(const void* a, const void* w, const void* bias, int64_t
   if (a == nullptr || w == nullptr || out == nullptr) return fail(1, "b2_linear_fwd: null pointer argument");
   if (m < 0 || n <= 0 || k <= 0) return fail(1, "b2_linear_fwd: invalid shape m=%lld n=%lld k=%lld", (long long)m,
                                              (long long)n, (long long)k);
-  if (epilogue < 0 || epilogue > 6) return fail(1, "b2_linear_fwd: unknown epilogue %d", epilogue);
+  if (epilogue < 0 || epilogue > 4)
+    return fail(1, "b2_linear_fwd: unknown epilogue %d (reduce-scatter epilogues go through b2_linear_rs_fwd)",
+                epilogue);
   if (n % 32 != 0) return fail(2, "b2_linear_fwd: n=%lld must be a multiple of 32", (long long)n);
   if (k % 8 != 0) return fail(2, "b2_linear_fwd: k=%lld must be a multiple of 8", (long long)k);
   if (ldo < n || ldo % 8 != 0) return fail(2, "b2_linear_fwd: ldo=%lld must be >= n and a multiple of 8", (long long)ldo);
@@ -224,4 +226,56 @@ B2_API int b2_peer_barrier(void* const* pads, int world, int rank, int channel, 
   if (world == 1) return 0;
   return check_launch(launch_peer_barrier(p, world, rank, channel, static_cast<cudaStream_t>(stream)),
                       "b2_peer_barrier");
+}
+
+B2_API int b2_linear_rs_fwd(const void* a, const void* w, const void* bias, int64_t m, int64_t n, int64_t k,
+                            int zero_masked_rows, void* const* peer_resid, int world, int rank, int64_t rows_per_rank,
+                            int64_t ldo, const uint8_t* row_mask, int tile_n, void* stream) {
+  if (a == nullptr || w == nullptr || peer_resid == nullptr) return fail(1, "b2_linear_rs_fwd: null pointer argument");
+  if (m < 0 || n <= 0 || k <= 0) return fail(1, "b2_linear_rs_fwd: invalid shape");
+  if (world < 1 || world > kGemmMaxPeers || rank < 0 || rank >= world)
+    return fail(1, "b2_linear_rs_fwd: rank %d / world %d invalid (world <= %d)", rank, world, kGemmMaxPeers);
+  if (rows_per_rank <= 0 || rows_per_rank * world < m) return fail(1, "b2_linear_rs_fwd: rows_per_rank too small");
+  if (n % 32 != 0 || k % 8 != 0 || ldo < n || ldo % 8 != 0)
+    return fail(2, "b2_linear_rs_fwd: n %% 32, k %% 8, ldo >= n and ldo %% 8 are required");
+  if ((tile_n & ~(kTilePair | 0xFFFF)) != 0) return fail(1, "b2_linear_rs_fwd: bad tile_n");
+  float* peers[kGemmMaxPeers] = {};
+  for (int r = 0; r < world; ++r) {
+    if (peer_resid[r] == nullptr || !aligned16(peer_resid[r]))
+      return fail(2, "b2_linear_rs_fwd: residual of rank %d is null or not 16-byte aligned", r);
+    peers[r] = static_cast<float*>(peer_resid[r]);
+  }
+  if (!aligned16(a) || !aligned16(w) || (bias && !aligned16(bias)))
+    return fail(2, "b2_linear_rs_fwd: pointers must be 16-byte aligned");
+  if (m == 0) return 0;
+  if (!is_sm100(nullptr)) return fail(2, "b2_linear_rs_fwd: needs an sm_100 (B200) device");
+  return check_launch(launch_gemm(static_cast<const __nv_bfloat16*>(a), static_cast<const __nv_bfloat16*>(w),
+                                  static_cast<const __nv_bfloat16*>(bias), m, n, k,
+                                  zero_masked_rows ? kEpiRsResidualZero : kEpiRsResidual, peers[rank], ldo, row_mask,
+                                  tile_n, static_cast<cudaStream_t>(stream), peers, world, rank, rows_per_rank),
+                      "b2_linear_rs_fwd");
+}
+
+B2_API int b2_layernorm_gather_fwd(const float* x, const void* gamma, const void* beta, float eps,
+                                   void* const* y_ranks, int world, const uint8_t* row_mask, int64_t rows,
+                                   int64_t d_model, void* stream) {
+  if (x == nullptr || gamma == nullptr || beta == nullptr || y_ranks == nullptr)
+    return fail(1, "b2_layernorm_gather_fwd: null pointer argument");
+  if (rows < 0 || d_model <= 0 || !(eps > 0.f)) return fail(1, "b2_layernorm_gather_fwd: invalid arguments");
+  if (world < 1 || world > kGatherMaxRanks) return fail(1, "b2_layernorm_gather_fwd: world %d not in [1, 8]", world);
+  if (!layernorm_gather_supported(d_model))
+    return fail(2, "b2_layernorm_gather_fwd: d_model=%lld not supported (256 * {1,2,3,4,8,16})", (long long)d_model);
+  GatherDst dst{};
+  for (int r = 0; r < world; ++r) {
+    if (y_ranks[r] == nullptr || !aligned16(y_ranks[r]))
+      return fail(2, "b2_layernorm_gather_fwd: destination of rank %d is null or not 16-byte aligned", r);
+    dst.rank_rows[r] = static_cast<__nv_bfloat16*>(y_ranks[r]);
+  }
+  if (!aligned16(x) || !aligned16(gamma) || !aligned16(beta))
+    return fail(2, "b2_layernorm_gather_fwd: pointers must be 16-byte aligned");
+  if (rows == 0) return 0;
+  return check_launch(launch_layernorm_gather(x, static_cast<const __nv_bfloat16*>(gamma),
+                                              static_cast<const __nv_bfloat16*>(beta), eps, dst, world, row_mask, rows,
+                                              d_model, static_cast<cudaStream_t>(stream)),
+                      "b2_layernorm_gather_fwd");
 }

@@ -539,20 +539,15 @@ __device__ __forceinline__ void pdl_wait_previous_grid() { asm volatile("griddep
 __device__ __forceinline__ void pdl_allow_next_grid() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------------------------
-// NVLink SHARP (NVLS) multicast memory: one operation on a multicast address reaches the same
-// offset of every GPU's copy through the NVSwitch.
+// Cross-GPU memory operations (tensor parallel): system-scope ordering and atomics on memory that
+// may belong to a peer GPU (mapped over NVLink).
 // ---------------------------------------------------------------------------------------------
-__device__ __forceinline__ void multimem_red_add_v4(float* mc, float a, float b, float c, float d) {
-  asm volatile("multimem.red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "f"(a), "f"(b),
-               "f"(c), "f"(d)
-               : "memory");
-}
-__device__ __forceinline__ void multimem_st_v4(float* mc, float a, float b, float c, float d) {
-  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "f"(a), "f"(b), "f"(c),
-               "f"(d)
-               : "memory");
-}
 __device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+// fp32 atomic add of 4 values, system scope (the address may be a peer GPU's memory).
+__device__ __forceinline__ void red_add_v4_sys(float* p, float a, float b, float c, float d) {
+  asm volatile("red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
 
 // ---------------------------------------------------------------------------------------------
 // Small numeric helpers

@@ -9,13 +9,12 @@
 //   kEpiResidual      res_f32  = mask ? res + acc + bias : res           (out_proj, masked_fill :78-79, x + a :733)
 //   kEpiResidualZero  res_f32  = mask ? res + acc + bias : 0             (ffn_out, x + f :734, masked_fill :736-737)
 //   kEpiStoreF32      out_f32  = acc (+ bias when given)                 (tensor-parallel partial sums)
-//   kEpiMcResidual    res_f32 += acc (+ bias) on every GPU, kept rows     (tensor parallel, fused all-reduce)
-//   kEpiMcResidualZero  same, and masked rows set to 0 on every GPU
-// The two kEpiMc* epilogues take `out` as an NVLS multicast address of the replicated fp32
-// residual: each rank's partial tile is added into every rank's copy by multimem.red through the
-// NVSwitch while the rest of the GEMM still runs, so the reduction needs no separate collective.
-// The caller passes the bias on one rank only and orders reads of the residual with cross-GPU
-// barriers before and after the GEMM.
+//   kEpiRsResidual    owner(row).res_f32 += acc (+ bias), kept rows       (tensor parallel, fused reduce-scatter)
+//   kEpiRsResidualZero  same, and masked rows set to 0 by their owner
+// The two kEpiRs* epilogues add each output row into the fp32 residual of the tensor-parallel
+// rank that owns the row (row / rows_per_rank) with system-scope atomics, over NVLink for the
+// other ranks' rows, while the rest of the GEMM still runs; the caller passes the bias on one
+// rank only and orders the owners' reads with cross-GPU barriers before and after the GEMM.
 // A is [M, K] row-major bf16 (tokens x features), W is [N, K] row-major bf16 (nn.Linear layout,
 // i.e. K-major for the B operand), the residual stream is fp32 [M, ldo].
 //
@@ -28,6 +27,7 @@
 //               op, stores to global memory.
 // Two TMEM accumulators (2 x BN fp32 columns) let the epilogue of tile i overlap the main loop
 // of tile i+1.
+#include <cstring>
 #include <mutex>
 
 #pragma once
@@ -41,9 +41,11 @@ enum GemmEpilogue : int {
   kEpiResidual = 2,
   kEpiResidualZero = 3,
   kEpiStoreF32 = 4,
-  kEpiMcResidual = 5,
-  kEpiMcResidualZero = 6,
+  kEpiRsResidual = 5,
+  kEpiRsResidualZero = 6,
 };
+
+constexpr int kGemmMaxPeers = 8;
 
 struct GemmParams {
   void* out;
@@ -52,6 +54,9 @@ struct GemmParams {
   const uint8_t* row_mask;
   int M, N, K;
   int m_blocks, n_blocks, k_blocks;
+  // kEpiRs*: every rank's residual base (as mapped here); row r belongs to rank r / rows_per_rank.
+  float* peer_out[kGemmMaxPeers];
+  int rows_per_rank, world, rank;
 };
 
 constexpr int kGemmBM = 128;
@@ -72,13 +77,13 @@ struct GemmCfg {
 };
 
 template <int EPI>
-__host__ __device__ constexpr bool is_mc_epi() {
-  return EPI == kEpiMcResidual || EPI == kEpiMcResidualZero;
+__host__ __device__ constexpr bool is_rs_epi() {
+  return EPI == kEpiRsResidual || EPI == kEpiRsResidualZero;
 }
 
 // Epilogue staging: TMEM gives each lane one row of the accumulator, so a lane writing its own
 // row would make every warp-wide global access touch 32 different rows (32 memory transactions
-// of 16 bytes per instruction, and for the multicast epilogues 32 NVLink requests). Each epilogue
+// of 16 bytes per instruction, and for the reduce-scatter epilogues 32 NVLink requests). Each epilogue
 // warp therefore passes its 32 x 32 fp32 chunk through 4 KB of shared memory and then works on
 // whole row segments: lane i handles columns 4(i % 8) .. +3 of rows i / 8, 4 + i / 8, ...
 constexpr int kEpiStageBytes = (kGemmThreads / 32 - 2) * 32 * 32 * 4;
@@ -163,12 +168,14 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmParams& p, int row
             make_uint2(pack_bf16x2(w.x, w.y), pack_bf16x2(w.z, w.w));
       } else if constexpr (EPI == kEpiStoreF32) {
         *reinterpret_cast<float4*>(static_cast<float*>(p.out) + off) = v[i];
-      } else {  // multicast: every GPU's copy of the residual
-        float* dst = static_cast<float*>(p.out) + off;
+      } else {  // reduce-scatter: the row owner's copy
+        const int row = row0 + i * 4 + (lane >> 3);
+        const int owner = min(row / p.rows_per_rank, p.world - 1);
+        float* dst = p.peer_out[owner] + off;
         if (keep[i])
-          multimem_red_add_v4(dst, v[i].x, v[i].y, v[i].z, v[i].w);
-        else if constexpr (EPI == kEpiMcResidualZero)
-          multimem_st_v4(dst, 0.f, 0.f, 0.f, 0.f);
+          red_add_v4_sys(dst, v[i].x, v[i].y, v[i].z, v[i].w);
+        else if (EPI == kEpiRsResidualZero && owner == p.rank)
+          *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
   }
@@ -344,7 +351,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_before_sync();
       mbar_arrive(&acc_empty[acc]);
     }
-    if constexpr (EPI == kEpiMcResidual || EPI == kEpiMcResidualZero) fence_acq_rel_sys();
+    if constexpr (is_rs_epi<EPI>()) fence_acq_rel_sys();
   }
 
   __syncthreads();
@@ -528,7 +535,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       tc_fence_before_sync();
       mbar_arrive_cluster(acc ? acc_empty_leader1 : acc_empty_leader0);
     }
-    if constexpr (EPI == kEpiMcResidual || EPI == kEpiMcResidualZero) fence_acq_rel_sys();
+    if constexpr (is_rs_epi<EPI>()) fence_acq_rel_sys();
   }
 
   if (*abort_flag && threadIdx.x == 0) {
@@ -600,10 +607,10 @@ static cudaError_t dispatch_epi2(int epi, const CUtensorMap& ta, const CUtensorM
       return launch_gemm2_t<BN, kEpiResidualZero>(ta, tb, p, grid, stream);
     case kEpiStoreF32:
       return launch_gemm2_t<BN, kEpiStoreF32>(ta, tb, p, grid, stream);
-    case kEpiMcResidual:
-      return launch_gemm2_t<BN, kEpiMcResidual>(ta, tb, p, grid, stream);
-    case kEpiMcResidualZero:
-      return launch_gemm2_t<BN, kEpiMcResidualZero>(ta, tb, p, grid, stream);
+    case kEpiRsResidual:
+      return launch_gemm2_t<BN, kEpiRsResidual>(ta, tb, p, grid, stream);
+    case kEpiRsResidualZero:
+      return launch_gemm2_t<BN, kEpiRsResidualZero>(ta, tb, p, grid, stream);
     default:
       return cudaErrorInvalidValue;
   }
@@ -623,10 +630,10 @@ static cudaError_t dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMa
       return launch_gemm_t<BN, kEpiResidualZero>(ta, tb, p, grid, stream);
     case kEpiStoreF32:
       return launch_gemm_t<BN, kEpiStoreF32>(ta, tb, p, grid, stream);
-    case kEpiMcResidual:
-      return launch_gemm_t<BN, kEpiMcResidual>(ta, tb, p, grid, stream);
-    case kEpiMcResidualZero:
-      return launch_gemm_t<BN, kEpiMcResidualZero>(ta, tb, p, grid, stream);
+    case kEpiRsResidual:
+      return launch_gemm_t<BN, kEpiRsResidual>(ta, tb, p, grid, stream);
+    case kEpiRsResidualZero:
+      return launch_gemm_t<BN, kEpiRsResidualZero>(ta, tb, p, grid, stream);
     default:
       return cudaErrorInvalidValue;
   }
@@ -668,7 +675,8 @@ int gemm_pick_tile(int M, int N, int sm_count) {
 
 cudaError_t launch_gemm(const __nv_bfloat16* A, const __nv_bfloat16* W, const __nv_bfloat16* bias, int64_t M,
                         int64_t N, int64_t K, int epi, void* out, int64_t ldo, const uint8_t* row_mask, int tile,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, float* const* peer_out = nullptr, int world = 1, int rank = 0,
+                        int64_t rows_per_rank = 0) {
   int dev = 0;
   cudaGetDevice(&dev);
   const int sms = device_sm_count(dev);
@@ -681,6 +689,11 @@ cudaError_t launch_gemm(const __nv_bfloat16* A, const __nv_bfloat16* W, const __
   e = make_tmap_bf16_2d(&tb, W, K, N, K * 2, kGemmBK, pair ? bn / 2 : bn);
   if (e != cudaSuccess) return e;
   GemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  for (int r = 0; peer_out != nullptr && r < world; ++r) p.peer_out[r] = peer_out[r];
+  p.world = world;
+  p.rank = rank;
+  p.rows_per_rank = static_cast<int>(rows_per_rank);
   p.out = out;
   p.ldo = ldo;
   p.bias = bias;

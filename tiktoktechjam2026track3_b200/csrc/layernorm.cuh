@@ -331,4 +331,110 @@ cudaError_t launch_layernorm(const void* x, int x_is_bf16, const __nv_bfloat16* 
   return launch_layernorm_t<false>(x, gamma, beta, eps, y, nullptr, row_mask, rows, D, stream);
 }
 
+// ---------------------------------------------------------------------------------------------
+// Tensor-parallel all-gather fused into LayerNorm: this rank normalises its own rows (fp32 in)
+// and writes the bf16 result into the same rows of every rank's LayerNorm buffer — local stores
+// for its own copy, NVLink peer stores for the others, 16 bytes per lane (a lane owns 8
+// consecutive columns of each 256-column group), so each GPU receives only the other ranks'
+// rows. D = 256 * NG. One warp per row; masked rows are written as 0.
+// ---------------------------------------------------------------------------------------------
+constexpr int kGatherMaxRanks = 8;
+struct GatherDst {
+  __nv_bfloat16* rank_rows[kGatherMaxRanks];  // each rank's destination for row 0 of this call
+};
+
+template <int NG>
+__global__ void __launch_bounds__(kLnWarpsPerBlock * 32)
+    layernorm_gather_kernel(const float* __restrict__ x, const __nv_bfloat16* __restrict__ gamma,
+                            const __nv_bfloat16* __restrict__ beta, float eps, GatherDst dst, int world,
+                            const uint8_t* __restrict__ row_mask, int64_t rows) {
+  pdl_wait_previous_grid();
+  pdl_allow_next_grid();
+  constexpr int D = NG * 256;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kLnWarpsPerBlock + (threadIdx.x >> 5);
+  if (row < rows) {
+    uint4 out[NG];
+    if (row_mask != nullptr && row_mask[row] == 0) {
+#pragma unroll
+      for (int g = 0; g < NG; ++g) out[g] = make_uint4(0u, 0u, 0u, 0u);
+    } else {
+      float v[NG][8];
+      const float4* xr = reinterpret_cast<const float4*>(x + row * D);
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {
+        const float4 a = __ldg(xr + g * 64 + lane * 2);
+        const float4 b = __ldg(xr + g * 64 + lane * 2 + 1);
+        v[g][0] = a.x, v[g][1] = a.y, v[g][2] = a.z, v[g][3] = a.w;
+        v[g][4] = b.x, v[g][5] = b.y, v[g][6] = b.z, v[g][7] = b.w;
+      }
+      float s = 0.f;
+#pragma unroll
+      for (int g = 0; g < NG; ++g)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s += v[g][j];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      const float mean = s * (1.0f / D);
+      float q = 0.f;
+#pragma unroll
+      for (int g = 0; g < NG; ++g)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float d = v[g][j] - mean;
+          q = fmaf(d, d, q);
+        }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+      const float rstd = rsqrtf(q * (1.0f / D) + eps);
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {
+        const uint4 graw = __ldg(reinterpret_cast<const uint4*>(gamma) + g * 32 + lane);
+        const uint4 braw = __ldg(reinterpret_cast<const uint4*>(beta) + g * 32 + lane);
+        const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&graw);
+        const __nv_bfloat162* bh = reinterpret_cast<const __nv_bfloat162*>(&braw);
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float o0 = fmaf((v[g][2 * j] - mean) * rstd, __low2float(gh[j]), __low2float(bh[j]));
+          const float o1 = fmaf((v[g][2 * j + 1] - mean) * rstd, __high2float(gh[j]), __high2float(bh[j]));
+          w[j] = pack_bf16x2(o0, o1);
+        }
+        out[g] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+    for (int r = 0; r < world; ++r) {
+      uint4* yr = reinterpret_cast<uint4*>(dst.rank_rows[r] + row * D);
+#pragma unroll
+      for (int g = 0; g < NG; ++g) yr[g * 32 + lane] = out[g];
+    }
+  }
+  fence_acq_rel_sys();  // peer stores ordered before the barrier that publishes them
+}
+
+bool layernorm_gather_supported(int64_t D) { return D % 256 == 0 && D / 256 >= 1 && D / 256 <= 16; }
+
+cudaError_t launch_layernorm_gather(const float* x, const __nv_bfloat16* gamma, const __nv_bfloat16* beta, float eps,
+                                    const GatherDst& dst, int world, const uint8_t* row_mask, int64_t rows, int64_t D,
+                                    cudaStream_t stream) {
+  const dim3 block(kLnWarpsPerBlock * 32);
+  const dim3 grid(static_cast<unsigned>((rows + kLnWarpsPerBlock - 1) / kLnWarpsPerBlock));
+  switch (D / 256) {
+    case 1:
+      return launch_pdl(layernorm_gather_kernel<1>, grid, block, 0, stream, x, gamma, beta, eps, dst, world, row_mask, rows);
+    case 2:
+      return launch_pdl(layernorm_gather_kernel<2>, grid, block, 0, stream, x, gamma, beta, eps, dst, world, row_mask, rows);
+    case 3:
+      return launch_pdl(layernorm_gather_kernel<3>, grid, block, 0, stream, x, gamma, beta, eps, dst, world, row_mask, rows);
+    case 4:
+      return launch_pdl(layernorm_gather_kernel<4>, grid, block, 0, stream, x, gamma, beta, eps, dst, world, row_mask, rows);
+    case 8:
+      return launch_pdl(layernorm_gather_kernel<8>, grid, block, 0, stream, x, gamma, beta, eps, dst, world, row_mask, rows);
+    case 16:
+      return launch_pdl(layernorm_gather_kernel<16>, grid, block, 0, stream, x, gamma, beta, eps, dst, world, row_mask, rows);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
 }  // namespace b2

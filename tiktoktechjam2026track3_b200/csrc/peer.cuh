@@ -1,8 +1,9 @@
-// Cross-GPU barrier over peer memory (NVLink P2P), for the tensor-parallel path whose all-reduce
-// is fused into the GEMM epilogues (kEpiMcResidual*): the residual stream is replicated in
-// symmetric memory and every rank adds its partial tiles into every copy through the NVSwitch,
-// so ranks must agree on two points per residual sub-block: "nobody reads the residual any more"
-// (before the first add) and "every add into my copy has landed" (before the next read).
+// Cross-GPU barrier over peer memory (NVLink P2P), for the tensor-parallel path whose
+// reduce-scatter is fused into the GEMM epilogues (kEpiRs*) and whose all-gather is fused into the
+// LayerNorm: ranks add their partial rows into the row owners' residuals and store LayerNorm rows
+// into every rank's buffer, so they must agree on "every add into my rows has landed" (before the
+// owner's LayerNorm reads them) and "every rank's LayerNorm rows have landed" (before the next
+// GEMM reads them).
 //
 // Each rank owns a pad of kPadChannels x kMaxPeers uint32 flags in memory every peer can map.
 // Slot [channel][src] of rank d's pad is written only by rank src and cleared only by rank d:
@@ -43,7 +44,7 @@ __global__ void __launch_bounds__(kMaxPeers, 1) peer_barrier_kernel(PeerPads pad
   if (r < world && r != rank) {
     uint32_t* to_peer = pads.pad[r] + channel * kMaxPeers + rank;
     uint32_t* from_peer = pads.pad[rank] + channel * kMaxPeers + r;
-    fence_sc_sys();  // this GPU's earlier writes (previous kernels, multimem adds) before the flag
+    fence_sc_sys();  // this GPU's earlier writes (previous kernels, peer adds and stores) before the flag
     const uint64_t t0 = global_timer_ns();
     bool ok = true;
     while (atom_cas_release_sys(to_peer, 0u, 1u) != 0u) {

@@ -15,12 +15,15 @@ are this build's own, one process per GPU with torch.distributed (NCCL) for the 
   per-rank partial sum [T, D] that has to be summed over ranks, one reduction per residual
   sub-block. Two ways to do it (`collective=`):
 
-  - "multimem" (default where the GPUs support NVLink SHARP multicast): the fp32 residual stream
-    is replicated in symmetric memory, and the out_proj / ffn_out GEMMs add their partial tiles
-    (plus the bias, on rank 0 only) straight into every rank's copy with multimem.red through the
-    NVSwitch (B2_EPI_MC_RESIDUAL*), tile by tile while the GEMM runs. The reduction and the
-    residual add happen inside the GEMM; four cross-GPU flag barriers per layer (b2_peer_barrier)
-    order the residual's readers (LayerNorms) against the adds.
+  - "rs" (default): the token rows are split over
+    the ranks (rank r owns rows [r T/n, (r+1) T/n)). The out_proj / ffn_out GEMMs add each output
+    row (plus the bias, on rank 0 only) into its owner's fp32 residual with system-scope atomics
+    over NVLink (b2_linear_rs_fwd: a reduce-scatter inside the GEMM epilogue); each owner then
+    LayerNorms only its rows and stores the bf16 result into every rank's LayerNorm buffer over
+    NVLink (b2_layernorm_gather_fwd: the all-gather inside the LayerNorm). Per
+    residual sub-block a GPU receives (n-1)/n of an fp32 [T, D] partial plus one bf16 [T, D] —
+    the reduce-scatter / all-gather volume — and the LayerNorm work drops by n. Four cross-GPU
+    flag barriers per layer (b2_peer_barrier) order readers against writers.
   - "nccl": each GEMM writes an fp32 partial, NCCL all-reduces it, and the fused residual +
     LayerNorm kernel (b2_add_layernorm_fwd) adds it with the bias. Kept as the baseline.
 """
@@ -114,13 +117,11 @@ class TensorParallelTransformer:
         self._mask_lengths = MaskLengths()
         self._launch_log: Optional[list] = None
         if collective == "auto":
-            collective = "multimem" if multicast_supported(device) and self.world > 1 else "nccl"
-        if collective not in ("multimem", "nccl"):
-            raise ValueError(f"collective must be 'auto', 'multimem' or 'nccl', not {collective!r}")
-        if collective == "multimem" and not multicast_supported(device):
-            raise RuntimeError("collective='multimem' needs NVLink SHARP multicast (symmetric memory) support")
+            collective = "rs" if self.world > 1 else "nccl"
+        if collective not in ("rs", "nccl"):
+            raise ValueError(f"collective must be 'auto', 'rs' or 'nccl', not {collective!r}")
         self.collective = collective
-        self._symm: Optional[Tuple[int, torch.Tensor, object, int, List[int]]] = None
+        self._symm_rs: Optional[dict] = None
 
     def record_launches(self, enabled: bool) -> None:
         """When enabled, every kernel launch and all-reduce is bracketed by CUDA events."""
@@ -148,41 +149,47 @@ class TensorParallelTransformer:
 
         dist.all_reduce(t, group=self.group)
 
-    def _symmetric_residual(self, tokens: int, d: int):
-        """fp32 residual [tokens, d] in symmetric memory plus the ranks' barrier pads.
-
-        Returns (resid, multicast address of resid, every rank's pad address). Allocated by a
-        collective rendezvous the first time a token count is seen, then reused.
-        """
-        if self._symm is not None and self._symm[0] == tokens:
-            return self._symm[1], self._symm[3], self._symm[4]
-        import torch.distributed as dist
-        import torch.distributed._symmetric_memory as symm_mem
-
-        self._symm = None
-        words = tokens * d + 64  # the pad sits after the residual, 256-byte aligned
-        buf = symm_mem.empty(words, dtype=torch.float32, device=self.device)
-        buf[tokens * d:].zero_()
-        group = self.group if self.group is not None else dist.group.WORLD
-        handle = symm_mem.rendezvous(buf, group)
-        mc = int(handle.multicast_ptr)
-        if mc == 0:
-            raise RuntimeError("symmetric memory has no multicast address on this device")
-        pads = [int(p) + tokens * d * 4 for p in handle.buffer_ptrs]
-        torch.cuda.synchronize(self.device)
-        dist.barrier(group=self.group)  # every pad is zero before any rank signals
-        self._symm = (tokens, buf[: tokens * d].view(tokens, d), handle, mc, pads)
-        return self._symm[1], mc, pads
-
     def _barrier(self, pads: List[int], channel: int) -> None:
         _capi.peer_barrier(pads, self.rank, channel, self.device)
 
+    def _rs_buffers(self, tokens: int, d: int) -> dict:
+        """Symmetric memory for the "rs" plan: fp32 residual [T, D], bf16 LayerNorm output [T, D]
+        and the barrier pads, in one allocation (rendezvous once per token count); only peer
+        mappings are used (no multicast)."""
+        if self._symm_rs is not None and self._symm_rs["tokens"] == tokens:
+            return self._symm_rs
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self._symm_rs = None
+        n_res = tokens * d  # fp32 words of the residual
+        n_ln = (tokens * d + 1) // 2  # fp32 words holding the bf16 LayerNorm rows
+        buf = symm_mem.empty(n_res + n_ln + 64, dtype=torch.float32, device=self.device)
+        buf[n_res + n_ln:].zero_()
+        group = self.group if self.group is not None else dist.group.WORLD
+        handle = symm_mem.rendezvous(buf, group)
+        bases = [int(p) for p in handle.buffer_ptrs]  # every rank's buffer, mapped over NVLink
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # every pad is zero before any rank signals
+        rows = -(-tokens // self.world)
+        self._symm_rs = {
+            "tokens": tokens, "buf": buf, "handle": handle,
+            "resid": buf[:n_res].view(tokens, d),
+            "ln": buf[n_res:n_res + n_ln].view(torch.bfloat16)[: tokens * d].view(tokens, d),
+            "ln_ranks": [b + n_res * 4 for b in bases],
+            "peer_resid": bases,
+            "pads": [b + (n_res + n_ln) * 4 for b in bases],
+            "rows_per_rank": rows,
+            "r0": min(tokens, self.rank * rows), "r1": min(tokens, (self.rank + 1) * rows),
+        }
+        return self._symm_rs
+
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
-        if self.collective == "multimem":
-            return self._forward_multimem(x, valid_token_mask)
+        if self.collective == "rs":
+            return self._forward_rs(x, valid_token_mask)
         return self._forward_nccl(x, valid_token_mask)
 
-    def _forward_multimem(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]) -> torch.Tensor:
+    def _forward_rs(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]) -> torch.Tensor:
         cfg = self.config
         if not x.is_cuda or x.dtype != torch.bfloat16:
             raise RuntimeError("TensorParallelTransformer needs a bf16 CUDA input")
@@ -197,38 +204,49 @@ class TensorParallelTransformer:
         d_loc = h_loc * hd
         f_loc = cfg.ffn_dim // n
         dev = x.device
-        resid, mc, pads = self._symmetric_residual(tokens, d)
-        ln = torch.empty(tokens, d, device=dev, dtype=torch.bfloat16)
+        sb = self._rs_buffers(tokens, d)
+        resid, ln, peers, pads = sb["resid"], sb["ln"], sb["peer_resid"], sb["pads"]
+        r0, r1, rpr = sb["r0"], sb["r1"], sb["rows_per_rank"]
+        my_resid = resid[r0:r1]
+        my_ln_rows = [base + r0 * d * 2 for base in sb["ln_ranks"]]
+        my_mask = row_mask[r0:r1] if row_mask is not None else None
         qkv = torch.empty(tokens, 3 * d_loc, device=dev, dtype=torch.bfloat16)
         ctx = torch.empty(tokens, d_loc, device=dev, dtype=torch.bfloat16)
         hidden = torch.empty(tokens, f_loc, device=dev, dtype=torch.bfloat16)
-        out = torch.empty(batch, seq_len, d, device=dev, dtype=torch.bfloat16)
         x2 = x.contiguous().view(tokens, d)
         lead = self.rank == 0  # adds the out_proj / ffn_out biases
         s0 = self.shards[0]
         t = self._timed
+        ch = 0
+
+        def barrier():
+            nonlocal ch
+            t("barrier", self._barrier, pads, ch)
+            ch = (ch + 1) % 4
+
+        # First LayerNorm on every rank for all rows (x is replicated): local, no exchange.
         t("layernorm", _capi.layernorm, x2, s0["ln1_w"], s0["ln1_b"], self.eps, ln, resid_out=resid)
+        barrier()  # every owner's residual rows exist before any rank adds into them
         for i, s in enumerate(self.shards):
             t("gemm_qkv", _capi.linear, ln, s["w_qkv"], s["b_qkv"], _capi.EPI_BIAS, qkv)
             t("attention", _capi.attention, qkv, batch, seq_len, h_loc, hd, 0, d_loc, 2 * d_loc, kv_len, cfg.causal,
               hd**-0.5, ctx)
-            t("barrier", self._barrier, pads, 0)  # every rank is done reading its residual copy
-            t("gemm_out", _capi.linear, ctx, s["w_o"], s["b_o"] if lead else None, _capi.EPI_MC_RESIDUAL, None,
-              row_mask, out_ptr=mc, out_ld=d)
-            t("barrier", self._barrier, pads, 1)  # every rank's adds have landed in every copy
-            t("layernorm", _capi.layernorm, resid, s["ln2_w"], s["ln2_b"], self.eps, ln)
+            t("gemm_out", _capi.linear_rs, ctx, s["w_o"], s["b_o"] if lead else None, False, peers, self.rank, rpr, d,
+              row_mask)
+            barrier()  # this rank's rows hold every rank's contribution
+            if r1 > r0:
+                t("layernorm", _capi.layernorm_gather, my_resid, s["ln2_w"], s["ln2_b"], self.eps, my_ln_rows)
+            barrier()  # every rank's LayerNorm rows landed in every copy
             t("gemm_ffn_in", _capi.linear, ln, s["w_1"], s["b_1"], _capi.EPI_BIAS_GELU, hidden)
-            t("barrier", self._barrier, pads, 2)
-            t("gemm_ffn_out", _capi.linear, hidden, s["w_2"], s["b_2"] if lead else None,
-              _capi.EPI_MC_RESIDUAL_ZERO, None, row_mask, out_ptr=mc, out_ld=d)
-            t("barrier", self._barrier, pads, 3)
-            if i == len(self.shards) - 1:
-                t("layernorm", _capi.layernorm, resid, self.final_w, self.final_b, self.eps, out.view(tokens, d),
-                  row_mask=row_mask)
-            else:
-                nxt = self.shards[i + 1]
-                t("layernorm", _capi.layernorm, resid, nxt["ln1_w"], nxt["ln1_b"], self.eps, ln)
-        return out
+            t("gemm_ffn_out", _capi.linear_rs, hidden, s["w_2"], s["b_2"] if lead else None, True, peers, self.rank,
+              rpr, d, row_mask)
+            barrier()
+            last = i == len(self.shards) - 1
+            g, b = (self.final_w, self.final_b) if last else (self.shards[i + 1]["ln1_w"], self.shards[i + 1]["ln1_b"])
+            if r1 > r0:
+                t("layernorm", _capi.layernorm_gather, my_resid, g, b, self.eps, my_ln_rows, my_mask if last else None)
+            barrier()
+        return ln.view(batch, seq_len, d).clone()
 
     def _forward_nccl(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]) -> torch.Tensor:
         cfg = self.config
@@ -278,22 +296,10 @@ class TensorParallelTransformer:
 
     def launches_per_forward(self, num_layers: int) -> int:
         """Kernels of this library per forward (NCCL's own kernels not counted)."""
-        return 1 + (11 if self.collective == "multimem" else 7) * num_layers
+        if self.collective == "rs":
+            return 2 + 11 * num_layers
+        return 1 + 7 * num_layers
 
     def close(self) -> None:
-        """Drops the symmetric-memory residual (call on every rank before destroying the group)."""
-        self._symm = None
-
-
-def multicast_supported(device: torch.device) -> bool:
-    """True when symmetric memory on `device` has an NVLink SHARP multicast address."""
-    try:
-        from torch._C._distributed_c10d import _SymmetricMemory
-        from torch._C._autograd import DeviceType
-    except ImportError:
-        return False
-    idx = torch.device(device).index or 0
-    try:
-        return bool(_SymmetricMemory.has_multicast_support(DeviceType.CUDA, idx))
-    except RuntimeError:
-        return False
+        """Drops the symmetric-memory buffers (call on every rank before destroying the group)."""
+        self._symm_rs = None
