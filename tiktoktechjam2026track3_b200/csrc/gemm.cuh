@@ -643,9 +643,14 @@ constexpr int kTilePair = 0x10000;  // tile code flag: 2-SM (CTA pair) variant
 
 // Picks the tile: the fraction of SM slots the tiles fill (waves rounded up) weighted by how well
 // the tile shape keeps the tensor core fed (operand bytes per MMA work; the 2-SM pair loads 1.5x
-// fewer bytes per FLOP and runs a deeper ring). 192-wide tiles exist for the D=768 projections:
-// 768 = 4 x 192 fills a wave at M=4096 where 256-wide tiles leave a third of the SMs idle.
-int gemm_pick_tile(int M, int N, int sm_count) {
+// fewer bytes per FLOP and runs a deeper ring). The pair's advantage is in the main loop; its
+// cluster launch and two-CTA handshakes are a fixed cost, so it only gets the bonus once a CTA
+// pair runs at least kPairMinKBlocks k-blocks (k-blocks per tile x waves) — on the 4096-token
+// C2 GEMMs (12-48 k-blocks per CTA) the one-CTA tiles measured 5-10% faster. 192-wide tiles exist
+// for the D=768 projections: 768 = 4 x 192 fills a wave at M=4096 where 256-wide tiles leave a
+// third of the SMs idle.
+int gemm_pick_tile(int M, int N, int K, int sm_count) {
+  constexpr long kPairMinKBlocks = 64;
   struct Cand {
     int code;
     int bn;
@@ -658,13 +663,16 @@ int gemm_pick_tile(int M, int N, int sm_count) {
                          {256, 256, kGemmBM, sm_count, 1.0},
                          {192, 192, kGemmBM, sm_count, 0.97},
                          {128, 128, kGemmBM, sm_count, 0.85}};
+  const long k_blocks = (K + kGemmBK - 1) / kGemmBK;
   int best = 128;
   double best_score = -1.0;
   for (const Cand& c : cands) {
     if (c.bn != 128 && N % c.bn != 0) continue;
     const long tiles = static_cast<long>((M + c.rows - 1) / c.rows) * ((N + c.bn - 1) / c.bn);
     const long waves = (tiles + c.slots - 1) / c.slots;
-    const double score = c.intensity * static_cast<double>(tiles) / static_cast<double>(waves * c.slots);
+    const bool pair = (c.code & kTilePair) != 0;
+    const double intensity = (pair && k_blocks * waves < kPairMinKBlocks) ? 0.95 : c.intensity;
+    const double score = intensity * static_cast<double>(tiles) / static_cast<double>(waves * c.slots);
     if (score > best_score + 1e-9) {
       best = c.code;
       best_score = score;
@@ -680,7 +688,7 @@ cudaError_t launch_gemm(const __nv_bfloat16* A, const __nv_bfloat16* W, const __
   int dev = 0;
   cudaGetDevice(&dev);
   const int sms = device_sm_count(dev);
-  if (tile == 0) tile = gemm_pick_tile(static_cast<int>(M), static_cast<int>(N), sms);
+  if (tile == 0) tile = gemm_pick_tile(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), sms);
   const bool pair = (tile & kTilePair) != 0;
   const int bn = tile & 0xFFFF;
   CUtensorMap ta, tb;
