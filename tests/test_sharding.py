@@ -16,7 +16,7 @@ import torch.nn.functional as F
 
 from oracle import reference_fp32 as oracle
 from tiktoktechjam2026track3_b200.cases import TransformerConfig
-from tiktoktechjam2026track3_b200.sharding import batch_shard, tp_check, tp_shard_state
+from tiktoktechjam2026track3_b200.sharding import batch_shard, rs_rows, tp_check, tp_shard_state
 
 
 def _free_port():
@@ -99,6 +99,91 @@ def test_tensor_parallel_math_matches_full_model_over_gloo(pad):
     q = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=_tp_rank, args=(r, world, port, cfg, pad, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    errs = dict(q.get(timeout=5) for _ in range(world))
+    assert max(errs.values()) < 1e-4, errs
+
+
+@pytest.mark.parametrize("tokens,world", [(80, 2), (81, 2), (7, 3), (1, 4), (32768, 8)])
+def test_rs_rows_partition_the_tokens(tokens, world):
+    spans = [rs_rows(tokens, world, r) for r in range(world)]
+    assert spans[0][0] == 0 and spans[-1][1] == tokens
+    for (a0, a1, per), (b0, _, _) in zip(spans, spans[1:]):
+        assert a1 == b0 and a1 - a0 <= per
+    per = spans[0][2]
+    for row in range(tokens):  # the GEMM epilogue's owner rule agrees with the spans
+        owner = min(row // per, world - 1)
+        assert spans[owner][0] <= row < spans[owner][1]
+
+
+def _rs_rank(rank, world, port, cfg, pad, result_queue):
+    """The "rs" plan's step sequence (TensorParallelTransformer._forward_rs) with fp32 torch ops:
+    partial rows reduced onto their owners (bias on rank 0), LayerNorm of the owned rows only,
+    rows gathered to every rank."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        state = oracle.build_reference_state(cfg, 0)
+        x, mask = oracle.generate_random_case(cfg, torch.device("cpu"), torch.float32, 3, pad)
+        shards = tp_shard_state(state, cfg, world, rank)
+        h_loc, hd = cfg.num_heads // world, cfg.d_model // cfg.num_heads
+        d_loc = h_loc * hd
+        b, s, d = x.shape
+        tokens = b * s
+        spans = [rs_rows(tokens, world, r) for r in range(world)]
+        r0, r1, _ = spans[rank]
+        m = mask.reshape(-1, 1)
+        lead = rank == 0
+
+        def ln(t, w, bb):
+            return F.layer_norm(t, (d,), w, bb, 1e-5)
+
+        def reduce_to_owners(part):  # every rank's partial rows summed onto the row owner
+            dist.all_reduce(part)  # (gloo has no reduce-scatter of uneven rows)
+            return part[r0:r1]
+
+        def gather_rows(rows_local):  # gloo gathers equal sizes: pad to rows_per_rank, then trim
+            per = spans[0][2]
+            padded = torch.zeros(per, d)
+            padded[: rows_local.shape[0]] = rows_local
+            out = [torch.zeros(per, d) for _ in range(world)]
+            dist.all_gather(out, padded)
+            return torch.cat([o[: spans[r][1] - spans[r][0]] for r, o in enumerate(out)], 0)
+
+        resid = x.reshape(-1, d).clone()[r0:r1]  # this rank's rows of the residual
+        y = ln(x.reshape(-1, d), shards[0]["ln1_w"], shards[0]["ln1_b"])  # first LayerNorm: all rows
+        mine = m[r0:r1]
+        for i, sh in enumerate(shards):
+            qkv = y @ sh["w_qkv"].T + sh["b_qkv"]
+            q, k, v = (qkv[:, j * d_loc:(j + 1) * d_loc].reshape(b, s, h_loc, hd).transpose(1, 2) for j in range(3))
+            ctx = oracle.attention_core(q, k, v, mask, cfg.causal, hd**-0.5).transpose(1, 2).reshape(-1, d_loc)
+            part = ctx @ sh["w_o"].T + (sh["b_o"] if lead else 0.0)
+            resid = torch.where(mine, resid + reduce_to_owners(torch.where(m, part, 0.0)), resid)
+            y = gather_rows(ln(resid, sh["ln2_w"], sh["ln2_b"]))
+            part = F.gelu(y @ sh["w_1"].T + sh["b_1"]) @ sh["w_2"].T + (sh["b_2"] if lead else 0.0)
+            resid = torch.where(mine, resid + reduce_to_owners(torch.where(m, part, 0.0)), torch.zeros_like(resid))
+            last = i == len(shards) - 1
+            if last:
+                y = gather_rows(torch.where(mine, ln(resid, state["final_norm.weight"], state["final_norm.bias"]), 0.0))
+            else:
+                y = gather_rows(ln(resid, shards[i + 1]["ln1_w"], shards[i + 1]["ln1_b"]))
+        ref = oracle.forward(state, cfg, x, mask)
+        result_queue.put((rank, float((y.reshape(b, s, d) - ref).abs().max())))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("pad,world", [(0.0, 2), (0.4, 2), (0.4, 3)])
+def test_reduce_scatter_plan_matches_full_model_over_gloo(pad, world):
+    cfg = TransformerConfig(2, 41, 384, 6, 768, 2, True)  # 82 tokens: uneven row split
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rs_rank, args=(r, world, port, cfg, pad, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:

@@ -49,6 +49,15 @@ def batch_shard(batch: int, world: int, rank: int) -> Tuple[int, int]:
     return start, stop
 
 
+def rs_rows(tokens: int, world: int, rank: int) -> Tuple[int, int, int]:
+    """Rows [r0, r1) a rank owns in the reduce-scatter plan, and rows per rank (the last rank may
+    own fewer; row r belongs to rank min(r // rows_per_rank, world - 1))."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"invalid rank {rank} of world {world}")
+    per = max(1, -(-tokens // world))
+    return min(tokens, rank * per), min(tokens, (rank + 1) * per), per
+
+
 def tp_check(config: TransformerConfig, world: int) -> None:
     """Raises ValueError unless heads and FFN columns split evenly into 64-aligned shards."""
     cfg = config_from(config)
@@ -171,7 +180,7 @@ class TensorParallelTransformer:
         bases = [int(p) for p in handle.buffer_ptrs]  # every rank's buffer, mapped over NVLink
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)  # every pad is zero before any rank signals
-        rows = -(-tokens // self.world)
+        r0, r1, rows = rs_rows(tokens, self.world, self.rank)
         self._symm_rs = {
             "tokens": tokens, "buf": buf, "handle": handle,
             "resid": buf[:n_res].view(tokens, d),
@@ -179,8 +188,7 @@ class TensorParallelTransformer:
             "ln_ranks": [b + n_res * 4 for b in bases],
             "peer_resid": bases,
             "pads": [b + (n_res + n_ln) * 4 for b in bases],
-            "rows_per_rank": rows,
-            "r0": min(tokens, self.rank * rows), "r1": min(tokens, (self.rank + 1) * rows),
+            "rows_per_rank": rows, "r0": r0, "r1": r1,
         }
         return self._symm_rs
 
