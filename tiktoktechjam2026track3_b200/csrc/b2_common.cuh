@@ -75,12 +75,6 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
-__device__ __forceinline__ uint32_t lane_id() {
-  uint32_t l;
-  asm volatile("mov.u32 %0, %%laneid;" : "=r"(l));
-  return l;
-}
-
 // ---------------------------------------------------------------------------------------------
 // mbarrier
 // ---------------------------------------------------------------------------------------------
@@ -182,24 +176,6 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
   }
 }
 
-// Same contract as mbar_wait, but spins on the non-suspending test_wait: lower wake-up latency for
-// waits on the critical path of a pipeline (the thread is not parked by the hardware).
-__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                               uint32_t kernel_id, uint32_t site) {
-  if (mbar_test_wait(bar, parity)) return true;
-  PollTimeout poll;
-  poll.reset();
-  while (true) {
-    if (mbar_test_wait(bar, parity)) return true;
-    if (*abort) return false;
-    if (poll.expired()) {
-      record_status(kernel_id, site, kReasonTimeout);
-      *abort = 1;
-      return false;
-    }
-  }
-}
-
 // Named barrier over `nthreads` threads (a multiple of 32) with id `id` (1..15; 0 is
 // __syncthreads). The non-.aligned form, so lanes may arrive from divergent paths.
 __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t nthreads) {
@@ -210,12 +186,6 @@ __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t nthread
 // named_barrier_sync calls of other warps that complete the count.
 __device__ __forceinline__ void named_barrier_arrive(uint32_t id, uint32_t nthreads) {
   asm volatile("barrier.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
-}
-
-// Makes this thread's generic-proxy shared-memory writes visible to the async proxy
-// (TMA, tcgen05.mma operand reads).
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -410,20 +380,6 @@ __device__ __forceinline__ void tmem_load_32cols(uint32_t taddr, float* v) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
-
-// One fp32 column of this thread's TMEM lane (same convergence and wait rules as above).
-__device__ __forceinline__ float tmem_load_1col(uint32_t taddr) {
-  uint32_t r;
-  __syncwarp();
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];\n\t"
-      "tcgen05.wait::ld.sync.aligned;\n"
-      : "=r"(r)
-      : "r"(taddr)
-      : "memory");
-  return __uint_as_float(r);
-}
-
 
 // 128 consecutive fp32 columns of this thread's TMEM lane in one instruction (then wait).
 __device__ __forceinline__ void tmem_load_128cols(uint32_t taddr, float* v) {
