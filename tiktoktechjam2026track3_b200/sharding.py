@@ -254,7 +254,9 @@ class TensorParallelTransformer:
             if r1 > r0:
                 t("layernorm", _capi.layernorm_gather, my_resid, g, b, self.eps, my_ln_rows, my_mask if last else None)
             barrier()
-        return ln.view(batch, seq_len, d).clone()
+        out = ln.view(batch, seq_len, d).clone()
+        self._mask_lengths.raise_if_invalid()
+        return out
 
     def _forward_nccl(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]) -> torch.Tensor:
         cfg = self.config
@@ -298,6 +300,7 @@ class TensorParallelTransformer:
             flags = _capi.ADD_LN_ZERO_ROWS | (_capi.ADD_LN_ZERO_Y if last else 0)
             t("layernorm", _capi.add_layernorm, resid, part, s["b_2"], g, b, self.eps,
               out.view(tokens, d) if last else ln, row_mask, flags)
+        self._mask_lengths.raise_if_invalid()
         return out
 
     __call__ = forward
