@@ -113,6 +113,18 @@ int b2_attention_fwd(const void* qkv, int64_t ld_qkv, int64_t q_col, int64_t k_c
                      float scale, void* ctx, int64_t ld_ctx, void* stream);
 
 /*
+ * b2_attention_fwd for the query rows [q_begin, q_begin + q_count) of every sequence only (keys
+ * are all of the sequence's valid keys; the causal mask uses absolute positions). Used by context
+ * parallelism, where a rank owns some query chunks of a long sequence and holds every key.
+ * q_begin is a multiple of 128; q_count is too, unless the range ends at seq_len. Other context
+ * rows are not written.
+ */
+int b2_attention_rows_fwd(const void* qkv, int64_t ld_qkv, int64_t q_col, int64_t k_col, int64_t v_col,
+                          int64_t batch, int64_t seq_len, int64_t num_heads, int64_t head_dim, const int32_t* kv_len,
+                          int causal, float scale, int64_t q_begin, int64_t q_count, void* ctx, int64_t ld_ctx,
+                          void* stream);
+
+/*
  * Tensor-parallel reduce-scatter fused into a residual GEMM: out = A W^T (+ bias) is added with
  * fp32 atomics (system scope) into the residual copy of the rank that owns each row — rank
  * r / rows_per_rank — so after every rank's call each owner holds its rows' full sum. No

@@ -240,6 +240,32 @@ def test_attention_matches_fp32_reference(batch, seq, heads, hd, causal, lengths
     assert torch.isfinite(got).all()
 
 
+@pytest.mark.parametrize("hd,causal,q_begin,q_count", [(64, True, 256, 384), (64, True, 128, 256), (128, True, 384, 640),
+                                                       (64, False, 512, 512), (32, True, 128, 384), (128, True, 0, 256),
+                                                       (64, True, 896, 128)])
+def test_attention_query_row_range_matches_full(hd, causal, q_begin, q_count):
+    """b2_attention_rows_fwd writes exactly the requested query rows, bit-identical to the full run
+    (each query tile's arithmetic does not depend on which tiles share its CTA)."""
+    batch, seq, heads = 2, 1024, 2
+    if q_begin + q_count > seq:
+        q_count = seq - q_begin
+    d = heads * hd
+    g = _gen(7 + hd)
+    qkv = torch.randn(batch * seq, 3 * d, device="cuda", generator=g).bfloat16()
+    kv_len = torch.tensor([seq, 700], device="cuda", dtype=torch.int32)
+    full = torch.zeros(batch * seq, d, device="cuda", dtype=torch.bfloat16)
+    part = torch.full((batch * seq, d), 7.0, device="cuda", dtype=torch.bfloat16)
+    _capi.attention(qkv, batch, seq, heads, hd, 0, d, 2 * d, kv_len, causal, hd**-0.5, full)
+    _capi.attention(qkv, batch, seq, heads, hd, 0, d, 2 * d, kv_len, causal, hd**-0.5, part, q_rows=(q_begin, q_count))
+    full, part = full.view(batch, seq, d), part.view(batch, seq, d)
+    valid = [seq, 700]
+    for b in range(batch):
+        n = min(valid[b], q_begin + q_count) - q_begin
+        if n > 0:
+            assert torch.equal(part[b, q_begin:q_begin + n], full[b, q_begin:q_begin + n])
+    assert torch.all(part[:, :q_begin] == 7.0) and torch.all(part[:, q_begin + q_count:] == 7.0)
+
+
 def test_attention_reads_heads_at_column_offsets():
     """Q/K/V blocks at arbitrary 64-aligned column offsets of a wider row (tensor-parallel shards)."""
     batch, seq, heads, hd = 1, 256, 2, 64

@@ -15,7 +15,7 @@ from __future__ import annotations
 import ctypes
 import threading
 from pathlib import Path
-from typing import Optional
+from typing import Optional, Tuple
 
 import torch
 
@@ -50,6 +50,11 @@ SIGNATURES = {
     "b2_attention_fwd": (
         ctypes.c_int,
         [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, ctypes.c_int, ctypes.c_float, _vp, _i64, _vp],
+    ),
+    "b2_attention_rows_fwd": (
+        ctypes.c_int,
+        [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, ctypes.c_int, ctypes.c_float, _i64, _i64, _vp, _i64,
+         _vp],
     ),
     "b2_peer_barrier": (ctypes.c_int, [ctypes.POINTER(_vp), ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
     "b2_linear_rs_fwd": (
@@ -234,19 +239,33 @@ def attention(
     causal: bool,
     scale: float,
     ctx: torch.Tensor,
+    q_rows: Optional[Tuple[int, int]] = None,
 ) -> None:
-    """ctx = softmax(mask(q k^T * scale)) v per head (see b2_attention_fwd)."""
+    """ctx = softmax(mask(q k^T * scale)) v per head (see b2_attention_fwd).
+
+    q_rows = (q_begin, q_count) computes only those query rows of every sequence
+    (b2_attention_rows_fwd).
+    """
     _require(qkv, torch.bfloat16, "qkv")
     _require(ctx, torch.bfloat16, "ctx")
     if kv_len is not None:
         _require(kv_len, torch.int32, "kv_len")
         if kv_len.numel() != batch:
             raise ValueError("kv_len must have one entry per sequence")
-    status = load_library().b2_attention_fwd(
+    lib = load_library()
+    if q_rows is None:
+        status = lib.b2_attention_fwd(
+            _ptr(qkv), qkv.shape[-1], q_col, k_col, v_col, batch, seq_len, num_heads, head_dim, _ptr(kv_len),
+            1 if causal else 0, float(scale), _ptr(ctx), ctx.shape[-1], _stream_ptr(qkv.device),
+        )
+        _check(status, "b2_attention_fwd")
+        return
+    status = lib.b2_attention_rows_fwd(
         _ptr(qkv), qkv.shape[-1], q_col, k_col, v_col, batch, seq_len, num_heads, head_dim, _ptr(kv_len),
-        1 if causal else 0, float(scale), _ptr(ctx), ctx.shape[-1], _stream_ptr(qkv.device),
+        1 if causal else 0, float(scale), int(q_rows[0]), int(q_rows[1]), _ptr(ctx), ctx.shape[-1],
+        _stream_ptr(qkv.device),
     )
-    _check(status, "b2_attention_fwd")
+    _check(status, "b2_attention_rows_fwd")
 
 
 PAD_WORDS = 32  # kPadChannels x kMaxPeers uint32 flags per rank

@@ -31,7 +31,9 @@ struct AttnParams {
   int q_col, k_col, v_col;
   int causal;
   float scale_log2;  // head_dim^-0.5 * log2(e)
-  int n_q_tiles;
+  int n_q_tiles;     // query tiles of 128 rows computed per sequence, starting at tile q_tile0
+  int q_tile0;       // first query tile (queries are absolute positions for the causal mask)
+  int q_end;         // one past the last query row computed
 };
 
 // Softmax-warp wait: once any wait of this thread gave up (`alive` false) later waits are
@@ -56,7 +58,9 @@ static cudaError_t launch_attention_simt(const __nv_bfloat16* qkv, int64_t ld_qk
 
 cudaError_t launch_attention(const __nv_bfloat16* qkv, int64_t ld_qkv, int64_t q_col, int64_t k_col, int64_t v_col,
                              int64_t B, int64_t S, int64_t H, int64_t hd, const int32_t* kv_len, int causal,
-                             float scale, __nv_bfloat16* ctx, int64_t ld_ctx, cudaStream_t stream) {
+                             float scale, __nv_bfloat16* ctx, int64_t ld_ctx, cudaStream_t stream,
+                             int64_t q_begin = 0, int64_t q_count = -1) {
+  if (q_count < 0) q_count = S - q_begin;
   AttnParams p;
   p.ctx = ctx;
   p.ld_ctx = ld_ctx;
@@ -69,7 +73,9 @@ cudaError_t launch_attention(const __nv_bfloat16* qkv, int64_t ld_qkv, int64_t q
   p.v_col = static_cast<int>(v_col);
   p.causal = causal;
   p.scale_log2 = scale * 1.4426950408889634f;
-  p.n_q_tiles = static_cast<int>((S + 127) / 128);
+  p.q_tile0 = static_cast<int>(q_begin / 128);
+  p.q_end = static_cast<int>(q_begin + q_count);
+  p.n_q_tiles = static_cast<int>((q_count + 127) / 128);
   switch (hd) {
     case 8:
       return launch_attention_simt<8>(qkv, ld_qkv, p, stream);

@@ -131,14 +131,14 @@ __global__ void __launch_bounds__(AttnPairCfg<HD>::kThreads, 1)
   int n_kv[2];
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
-    const int qt = 2 * pair + t;
-    const bool live = qt < p.n_q_tiles && qt * 128 < kv_len;
+    const int qt = p.q_tile0 + 2 * pair + t;  // absolute query tile
+    const bool live = 2 * pair + t < p.n_q_tiles && qt * 128 < kv_len;
     n_kv[t] = live ? (p.causal ? min(qt + 1, kv_tiles) : kv_tiles) : 0;
   }
   const int n_total = max(n_kv[0], n_kv[1]);
   if (n_total == 0) return;  // uniform for the CTA: nothing allocated yet
   const int row_base = b * p.S;
-  const int q_row0 = row_base + pair * 256;
+  const int q_row0 = row_base + (p.q_tile0 + 2 * pair) * 128;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -346,7 +346,7 @@ __global__ void __launch_bounds__(AttnPairCfg<HD>::kThreads, 1)
     const int grp = (warp - Cfg::kSoftmaxWarp0) >> 2;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
-    const int qt = 2 * pair + grp;
+    const int qt = p.q_tile0 + 2 * pair + grp;
     const int query = qt * 128 + r;
     const int n = grp == 0 ? n_kv[0] : n_kv[1];
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
@@ -479,7 +479,7 @@ __global__ void __launch_bounds__(AttnPairCfg<HD>::kThreads, 1)
       for (int cc = 0; cc < HD / 32; ++cc) {
         float o[32];
         tmem_load_32cols(t_o + 32 * cc, o);
-        if (query < p.S) {
+        if (query < p.q_end) {
 #pragma unroll
           for (int k = 0; k < 4; ++k)
             dst[4 * cc + k] = make_uint4(pack_bf16x2(o[8 * k] * inv, o[8 * k + 1] * inv),

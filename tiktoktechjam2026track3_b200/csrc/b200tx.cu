@@ -14,6 +14,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <string>
 
 #include "b2_common.cuh"
 #include "layernorm.cuh"
@@ -161,32 +162,52 @@ B2_API int b2_linear_fwd(const void* a, const void* w, const void* bias, int64_t
                       "b2_linear_fwd");
 }
 
-B2_API int b2_attention_fwd(const void* qkv, int64_t ld_qkv, int64_t q_col, int64_t k_col, int64_t v_col,
-                            int64_t batch, int64_t seq_len, int64_t num_heads, int64_t head_dim, const int32_t* kv_len,
-                            int causal, float scale, void* ctx, int64_t ld_ctx, void* stream) {
-  if (qkv == nullptr || ctx == nullptr) return fail(1, "b2_attention_fwd: null pointer argument");
-  if (batch < 0 || seq_len < 0 || num_heads <= 0) return fail(1, "b2_attention_fwd: invalid shape");
+B2_API int b2_attention_rows_fwd(const void* qkv, int64_t ld_qkv, int64_t q_col, int64_t k_col, int64_t v_col,
+                                 int64_t batch, int64_t seq_len, int64_t num_heads, int64_t head_dim,
+                                 const int32_t* kv_len, int causal, float scale, int64_t q_begin, int64_t q_count,
+                                 void* ctx, int64_t ld_ctx, void* stream) {
+  if (qkv == nullptr || ctx == nullptr) return fail(1, "b2_attention_rows_fwd: null pointer argument");
+  if (batch < 0 || seq_len < 0 || num_heads <= 0) return fail(1, "b2_attention_rows_fwd: invalid shape");
   const bool tensor_core = head_dim == 64 || head_dim == 128;
   if (!tensor_core && head_dim != 8 && head_dim != 16 && head_dim != 32 && head_dim != 256)
-    return fail(2, "b2_attention_fwd: head_dim=%lld not supported (8, 16, 32, 64, 128, 256)", (long long)head_dim);
+    return fail(2, "b2_attention_rows_fwd: head_dim=%lld not supported (8, 16, 32, 64, 128, 256)", (long long)head_dim);
   const int64_t col_align = tensor_core ? 64 : 8;
   if (q_col % col_align || k_col % col_align || v_col % col_align || q_col < 0 || k_col < 0 || v_col < 0)
-    return fail(2, "b2_attention_fwd: q/k/v column offsets must be non-negative multiples of %lld",
+    return fail(2, "b2_attention_rows_fwd: q/k/v column offsets must be non-negative multiples of %lld",
                 (long long)col_align);
   const int64_t width = num_heads * head_dim;
   if (q_col + width > ld_qkv || k_col + width > ld_qkv || v_col + width > ld_qkv)
-    return fail(1, "b2_attention_fwd: q/k/v columns exceed ld_qkv");
-  if (ld_qkv % 8 != 0 || ld_ctx % 8 != 0 || ld_ctx < width) return fail(2, "b2_attention_fwd: bad leading dimensions");
-  if (!aligned16(qkv) || !aligned16(ctx)) return fail(2, "b2_attention_fwd: pointers must be 16-byte aligned");
+    return fail(1, "b2_attention_rows_fwd: q/k/v columns exceed ld_qkv");
+  if (ld_qkv % 8 != 0 || ld_ctx % 8 != 0 || ld_ctx < width) return fail(2, "b2_attention_rows_fwd: bad leading dimensions");
+  if (!aligned16(qkv) || !aligned16(ctx)) return fail(2, "b2_attention_rows_fwd: pointers must be 16-byte aligned");
   if (batch * seq_len > 0x7fffff00LL || batch * num_heads > 0x7fffffffLL || (seq_len + 127) / 128 > 65535)
-    return fail(2, "b2_attention_fwd: problem too large");
-  if (!(scale > 0.f)) return fail(1, "b2_attention_fwd: scale must be positive");
-  if (batch == 0 || seq_len == 0) return 0;
-  if (!is_sm100(nullptr)) return fail(2, "b2_attention_fwd: needs an sm_100 (B200) device");
+    return fail(2, "b2_attention_rows_fwd: problem too large");
+  if (!(scale > 0.f)) return fail(1, "b2_attention_rows_fwd: scale must be positive");
+  if (q_begin < 0 || q_count < 0 || q_begin + q_count > seq_len || q_begin % 128 != 0 ||
+      (q_count % 128 != 0 && q_begin + q_count != seq_len))
+    return fail(1, "b2_attention_rows_fwd: query rows [%lld, +%lld) must start on a multiple of 128 and end on one or at "
+                "seq_len", (long long)q_begin, (long long)q_count);
+  if (batch == 0 || seq_len == 0 || q_count == 0) return 0;
+  if (!is_sm100(nullptr)) return fail(2, "b2_attention_rows_fwd: needs an sm_100 (B200) device");
   return check_launch(launch_attention(static_cast<const __nv_bfloat16*>(qkv), ld_qkv, q_col, k_col, v_col, batch,
                                        seq_len, num_heads, head_dim, kv_len, causal, scale,
-                                       static_cast<__nv_bfloat16*>(ctx), ld_ctx, static_cast<cudaStream_t>(stream)),
-                      "b2_attention_fwd");
+                                       static_cast<__nv_bfloat16*>(ctx), ld_ctx, static_cast<cudaStream_t>(stream), q_begin,
+                                       q_count),
+                      "b2_attention_rows_fwd");
+}
+
+B2_API int b2_attention_fwd(const void* qkv, int64_t ld_qkv, int64_t q_col, int64_t k_col, int64_t v_col,
+                            int64_t batch, int64_t seq_len, int64_t num_heads, int64_t head_dim, const int32_t* kv_len,
+                            int causal, float scale, void* ctx, int64_t ld_ctx, void* stream) {
+  const int rc = b2_attention_rows_fwd(qkv, ld_qkv, q_col, k_col, v_col, batch, seq_len, num_heads, head_dim, kv_len,
+                                       causal, scale, 0, seq_len < 0 ? 0 : seq_len, ctx, ld_ctx, stream);
+  if (rc != 0) {
+    std::string msg = g_last_error;
+    const std::string from = "b2_attention_rows_fwd";
+    if (msg.compare(0, from.size(), from) == 0) msg = "b2_attention_fwd" + msg.substr(from.size());
+    snprintf(g_last_error, sizeof(g_last_error), "%s", msg.c_str());
+  }
+  return rc;
 }
 
 B2_API int b2_add_layernorm_fwd(float* resid, const float* delta, const void* bias, const uint8_t* row_mask,
