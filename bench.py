@@ -68,6 +68,8 @@ def parse_args(argv=None):
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--workload", default="c2", choices=sorted(BASELINE_CONFIGS))
     p.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    p.add_argument("--split", default="tp", choices=("tp", "cp"),
+                   help="batch smaller than the GPU count: head/FFN tensor parallel (tp) or context parallel (cp)")
     p.add_argument("--collective", default="auto", choices=("auto", "rs", "nccl"),
                    help="tensor-parallel reduction: reduce-scatter in the GEMMs + all-gather in the LayerNorm over "
                         "NVLink (rs), or NCCL all-reduce")
@@ -320,10 +322,13 @@ def main() -> None:
     # (strong scaling); everything else gives each rank its own batch shard (weak scaling).
     tensor_parallel = world > 1 and cfg.batch_size < world
     if tensor_parallel:
-        from tiktoktechjam2026track3_b200.sharding import TensorParallelTransformer
+        from tiktoktechjam2026track3_b200.sharding import ContextParallelTransformer, TensorParallelTransformer
 
         full = UserOptimizedTransformer(cfg)
-        model = TensorParallelTransformer(cfg, full.state_dict(), device, collective=args.collective)
+        if args.split == "cp":
+            model = ContextParallelTransformer(cfg, full.state_dict(), device)
+        else:
+            model = TensorParallelTransformer(cfg, full.state_dict(), device, collective=args.collective)
         del full
         x, mask = generate_random_case(cfg, device, torch.bfloat16, 100000, pad)
     else:
@@ -492,7 +497,11 @@ def main() -> None:
                 "layers": cfg.num_layers,
                 "causal": cfg.causal,
                 "padding_ratio": pad,
-                "parallelism": (f"tp{world} (heads / FFN columns; " + {
+                "parallelism": (f"cp{world} (each sequence's tokens in 2 x {world} zigzag chunks; Q/K/V rows "
+                                "all-gathered over NVLink into every GPU's full-length buffer, attention of the "
+                                "rank's query rows, LayerNorms and GEMMs on its own rows; 2 flag barriers per block)")
+                if tensor_parallel and model.collective == "cp" else
+                (f"tp{world} (heads / FFN columns; " + {
                     "rs": "out_proj / ffn_out GEMM epilogues add each row into its owner's fp32 residual over "
                           "NVLink (reduce-scatter), owners' LayerNorm rows stored into every GPU's buffer (all-gather), "
                           "4 flag barriers per block)",

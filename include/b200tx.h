@@ -113,15 +113,16 @@ int b2_attention_fwd(const void* qkv, int64_t ld_qkv, int64_t q_col, int64_t k_c
                      float scale, void* ctx, int64_t ld_ctx, void* stream);
 
 /*
- * b2_attention_fwd for the query rows [q_begin, q_begin + q_count) of every sequence only (keys
- * are all of the sequence's valid keys; the causal mask uses absolute positions). Used by context
- * parallelism, where a rank owns some query chunks of a long sequence and holds every key.
- * q_begin is a multiple of 128; q_count is too, unless the range ends at seq_len. Other context
- * rows are not written.
+ * b2_attention_fwd for some query rows of every sequence only: q_ranges holds n_ranges (1 or 2)
+ * pairs (q_begin, q_count); keys are all of the sequence's valid keys and the causal mask uses
+ * absolute positions. Used by context parallelism, where a rank owns two query chunks of a long
+ * sequence and holds every key (one launch for both; the later range's work is issued first).
+ * Each q_begin is a multiple of 128 and each q_count too, unless its range ends at seq_len; the
+ * second range starts after the first ends. Other context rows are not written.
  */
 int b2_attention_rows_fwd(const void* qkv, int64_t ld_qkv, int64_t q_col, int64_t k_col, int64_t v_col,
                           int64_t batch, int64_t seq_len, int64_t num_heads, int64_t head_dim, const int32_t* kv_len,
-                          int causal, float scale, int64_t q_begin, int64_t q_count, void* ctx, int64_t ld_ctx,
+                          int causal, float scale, const int64_t* q_ranges, int n_ranges, void* ctx, int64_t ld_ctx,
                           void* stream);
 
 /*
@@ -139,6 +140,20 @@ int b2_attention_rows_fwd(const void* qkv, int64_t ld_qkv, int64_t q_col, int64_
 int b2_linear_rs_fwd(const void* a, const void* w, const void* bias, int64_t m, int64_t n, int64_t k,
                      int zero_masked_rows, void* const* peer_resid, int world, int rank, int64_t rows_per_rank,
                      int64_t ldo, const uint8_t* row_mask, int tile_n, void* stream);
+
+/*
+ * b2_linear_fwd with epilogue B2_EPI_BIAS whose output columns [col_begin, n) are also stored into
+ * every other context-parallel rank's copy of the output (NVLink peer stores from the epilogue):
+ * the packed Q/K/V projection of a rank's token rows with K and V all-gathered on the fly. No
+ * counterpart in the reference (one GPU); replaces q/k/v_proj (models.py:51-53) plus the K/V
+ * exchange of context parallelism.
+ *   peer_out  host array of `world` device pointers: every rank's output [m, ldo] bf16 as mapped
+ *             into this process; the caller's is peer_out[rank]
+ * The caller orders the peers' reads of their outputs against these stores (b2_peer_barrier).
+ */
+int b2_linear_bcast_fwd(const void* a, const void* w, const void* bias, int64_t m, int64_t n, int64_t k,
+                        void* const* peer_out, int world, int rank, int64_t col_begin, int64_t ldo, int tile_n,
+                        void* stream);
 
 /*
  * LayerNorm of fp32 rows (x [rows, d_model]) written as bf16 into the same rows of every

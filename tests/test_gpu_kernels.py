@@ -256,7 +256,8 @@ def test_attention_query_row_range_matches_full(hd, causal, q_begin, q_count):
     full = torch.zeros(batch * seq, d, device="cuda", dtype=torch.bfloat16)
     part = torch.full((batch * seq, d), 7.0, device="cuda", dtype=torch.bfloat16)
     _capi.attention(qkv, batch, seq, heads, hd, 0, d, 2 * d, kv_len, causal, hd**-0.5, full)
-    _capi.attention(qkv, batch, seq, heads, hd, 0, d, 2 * d, kv_len, causal, hd**-0.5, part, q_rows=(q_begin, q_count))
+    _capi.attention(qkv, batch, seq, heads, hd, 0, d, 2 * d, kv_len, causal, hd**-0.5, part,
+                    q_rows=(q_begin, q_count))
     full, part = full.view(batch, seq, d), part.view(batch, seq, d)
     valid = [seq, 700]
     for b in range(batch):
@@ -264,6 +265,23 @@ def test_attention_query_row_range_matches_full(hd, causal, q_begin, q_count):
         if n > 0:
             assert torch.equal(part[b, q_begin:q_begin + n], full[b, q_begin:q_begin + n])
     assert torch.all(part[:, :q_begin] == 7.0) and torch.all(part[:, q_begin + q_count:] == 7.0)
+
+
+@pytest.mark.parametrize("hd", [64, 128, 32])
+def test_attention_two_query_ranges_match_full(hd):
+    """Two ranges in one launch (the context-parallel zigzag chunks) equal the full run on their rows."""
+    batch, seq, heads = 1, 2048, 2
+    d = heads * hd
+    g = _gen(11 + hd)
+    qkv = torch.randn(batch * seq, 3 * d, device="cuda", generator=g).bfloat16()
+    full = torch.zeros(seq, d, device="cuda", dtype=torch.bfloat16)
+    part = torch.full((seq, d), 7.0, device="cuda", dtype=torch.bfloat16)
+    _capi.attention(qkv, batch, seq, heads, hd, 0, d, 2 * d, None, True, hd**-0.5, full)
+    _capi.attention(qkv, batch, seq, heads, hd, 0, d, 2 * d, None, True, hd**-0.5, part,
+                    q_rows=[(256, 256), (1536, 256)])
+    for r0, n in [(256, 256), (1536, 256)]:
+        assert torch.equal(part[r0:r0 + n], full[r0:r0 + n])
+    assert torch.all(part[:256] == 7.0) and torch.all(part[512:1536] == 7.0) and torch.all(part[1792:] == 7.0)
 
 
 def test_attention_reads_heads_at_column_offsets():

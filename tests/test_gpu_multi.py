@@ -3,6 +3,7 @@
 * tensor parallel (heads/FFN columns) agrees with the single-GPU model within the parity gate
   (reduction order differs, so not bitwise), both with the reduce-scatter fused into the GEMM
   epilogues and the all-gather into the LayerNorm ("rs") and with the NCCL all-reduce;
+* context parallel (zigzag token chunks, K/V rows all-gathered over NVLink) agrees likewise;
 * a batch shard on rank r is bit-identical to the same sequences of the single-GPU run.
 """
 
@@ -18,7 +19,7 @@ import torch.multiprocessing as mp
 from oracle import reference_fp32 as oracle
 from tiktoktechjam2026track3_b200 import UserOptimizedTransformer, baseline_gate
 from tiktoktechjam2026track3_b200.cases import TransformerConfig
-from tiktoktechjam2026track3_b200.sharding import TensorParallelTransformer, batch_shard
+from tiktoktechjam2026track3_b200.sharding import ContextParallelTransformer, TensorParallelTransformer, batch_shard
 
 pytestmark = pytest.mark.gpu
 
@@ -41,14 +42,15 @@ def _worker(rank, world, port, cfg, pad, q):
         model = UserOptimizedTransformer(cfg)
         model.load_state_dict(state, strict=True)
         model = model.to(device=dev, dtype=torch.bfloat16).eval()
-        collectives = ["nccl", "rs"]
+        collectives = ["nccl", "rs", "cp"]
         with torch.inference_mode():
             single = model(xb, mask)
             b0, b1 = batch_shard(cfg.batch_size, world, rank)
             shard = model(xb[b0:b1].contiguous(), mask[b0:b1].contiguous())
             outs = {}
             for coll in collectives:
-                tp = TensorParallelTransformer(cfg, state, dev, collective=coll)
+                tp = (ContextParallelTransformer(cfg, state, dev) if coll == "cp" else
+                      TensorParallelTransformer(cfg, state, dev, collective=coll))
                 outs[coll] = tp(xb, mask)
                 outs[coll + "_again"] = tp(xb * 0.5, mask)
                 outs[coll + "_again_ref"] = model(xb * 0.5, mask)

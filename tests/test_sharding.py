@@ -16,7 +16,7 @@ import torch.nn.functional as F
 
 from oracle import reference_fp32 as oracle
 from tiktoktechjam2026track3_b200.cases import TransformerConfig
-from tiktoktechjam2026track3_b200.sharding import batch_shard, rs_rows, tp_check, tp_shard_state
+from tiktoktechjam2026track3_b200.sharding import batch_shard, cp_chunks, rs_rows, tp_check, tp_shard_state
 
 
 def _free_port():
@@ -118,6 +118,18 @@ def test_rs_rows_partition_the_tokens(tokens, world):
     for row in range(tokens):  # the GEMM epilogue's owner rule agrees with the spans
         owner = min(row // per, world - 1)
         assert spans[owner][0] <= row < spans[owner][1]
+
+
+@pytest.mark.parametrize("seq_len,world", [(32768, 2), (32768, 4), (32768, 8), (1024, 2)])
+def test_cp_chunks_cover_the_sequence_with_equal_causal_work(seq_len, world):
+    chunk, _ = cp_chunks(seq_len, world, 0)
+    owned = sorted(c for r in range(world) for c in cp_chunks(seq_len, world, r)[1])
+    assert owned == list(range(2 * world)) and chunk * 2 * world == seq_len
+    # causal work of chunk c is proportional to (c + 1/2): every rank's pair sums to the same
+    work = {sum(c + 0.5 for c in cp_chunks(seq_len, world, r)[1]) for r in range(world)}
+    assert len(work) == 1
+    with pytest.raises(ValueError):
+        cp_chunks(1000, 2, 0)
 
 
 def _rs_rank(rank, world, port, cfg, pad, result_queue):

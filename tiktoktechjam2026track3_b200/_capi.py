@@ -53,14 +53,19 @@ SIGNATURES = {
     ),
     "b2_attention_rows_fwd": (
         ctypes.c_int,
-        [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, ctypes.c_int, ctypes.c_float, _i64, _i64, _vp, _i64,
-         _vp],
+        [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, ctypes.c_int, ctypes.c_float, ctypes.POINTER(_i64),
+         ctypes.c_int, _vp, _i64, _vp],
     ),
     "b2_peer_barrier": (ctypes.c_int, [ctypes.POINTER(_vp), ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
     "b2_linear_rs_fwd": (
         ctypes.c_int,
         [_vp, _vp, _vp, _i64, _i64, _i64, ctypes.c_int, ctypes.POINTER(_vp), ctypes.c_int, ctypes.c_int, _i64, _i64,
          _vp, ctypes.c_int, _vp],
+    ),
+    "b2_linear_bcast_fwd": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _i64, _i64, _i64, ctypes.POINTER(_vp), ctypes.c_int, ctypes.c_int, _i64, _i64, ctypes.c_int,
+         _vp],
     ),
     "b2_layernorm_gather_fwd": (
         ctypes.c_int, [_vp, _vp, _vp, ctypes.c_float, ctypes.POINTER(_vp), ctypes.c_int, _vp, _i64, _i64, _vp],
@@ -239,12 +244,12 @@ def attention(
     causal: bool,
     scale: float,
     ctx: torch.Tensor,
-    q_rows: Optional[Tuple[int, int]] = None,
+    q_rows=None,
 ) -> None:
     """ctx = softmax(mask(q k^T * scale)) v per head (see b2_attention_fwd).
 
-    q_rows = (q_begin, q_count) computes only those query rows of every sequence
-    (b2_attention_rows_fwd).
+    q_rows = (q_begin, q_count), or a list of up to two such ranges in sequence order, computes
+    only those query rows of every sequence (b2_attention_rows_fwd).
     """
     _require(qkv, torch.bfloat16, "qkv")
     _require(ctx, torch.bfloat16, "ctx")
@@ -260,10 +265,11 @@ def attention(
         )
         _check(status, "b2_attention_fwd")
         return
+    ranges = [tuple(q_rows)] if isinstance(q_rows[0], int) else [tuple(r) for r in q_rows]
+    arr = (_i64 * (2 * len(ranges)))(*[int(v) for r in ranges for v in r])
     status = lib.b2_attention_rows_fwd(
         _ptr(qkv), qkv.shape[-1], q_col, k_col, v_col, batch, seq_len, num_heads, head_dim, _ptr(kv_len),
-        1 if causal else 0, float(scale), int(q_rows[0]), int(q_rows[1]), _ptr(ctx), ctx.shape[-1],
-        _stream_ptr(qkv.device),
+        1 if causal else 0, float(scale), arr, len(ranges), _ptr(ctx), ctx.shape[-1], _stream_ptr(qkv.device),
     )
     _check(status, "b2_attention_rows_fwd")
 
@@ -324,3 +330,23 @@ def layernorm_gather(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, e
         _stream_ptr(x.device),
     )
     _check(status, "b2_layernorm_gather_fwd")
+
+
+def linear_bcast(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], peer_out, rank: int, col_begin: int,
+                 ldo: int, tile_n: int = 0) -> None:
+    """out = bf16(a @ w.T + bias) into peer_out[rank], columns >= col_begin also into every other
+    rank's peer_out (see b2_linear_bcast_fwd). `peer_out` lists device addresses (ints)."""
+    _require(a, torch.bfloat16, "a")
+    _require(w, torch.bfloat16, "w")
+    m, k = a.shape
+    n = w.shape[0]
+    if w.shape[1] != k:
+        raise ValueError("a and w disagree on K")
+    if bias is not None:
+        _require(bias, torch.bfloat16, "bias")
+    arr = (_vp * len(peer_out))(*[int(x) for x in peer_out])
+    status = load_library().b2_linear_bcast_fwd(
+        _ptr(a), _ptr(w), _ptr(bias), m, n, k, arr, len(peer_out), int(rank), int(col_begin), int(ldo), int(tile_n),
+        _stream_ptr(a.device),
+    )
+    _check(status, "b2_linear_bcast_fwd")

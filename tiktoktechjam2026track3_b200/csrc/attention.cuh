@@ -31,10 +31,25 @@ struct AttnParams {
   int q_col, k_col, v_col;
   int causal;
   float scale_log2;  // head_dim^-0.5 * log2(e)
-  int n_q_tiles;     // query tiles of 128 rows computed per sequence, starting at tile q_tile0
-  int q_tile0;       // first query tile (queries are absolute positions for the causal mask)
-  int q_end;         // one past the last query row computed
+  // Query rows computed per sequence: up to two ranges (the second one later in the sequence, so
+  // its CTAs, the heavier ones under a causal mask, are issued first). Queries are absolute
+  // positions for the causal mask.
+  int n_ranges;
+  int q_tile0[2];    // first query tile (128 rows) of the range
+  int n_q_tiles[2];  // query tiles in the range
+  int q_end[2];      // one past the last query row of the range
 };
+
+// Query range of the CTA row `y` of a grid whose rows cover `per_range[r]` work items of range r,
+// range 1 first.
+__device__ __forceinline__ int attn_range_of(const AttnParams& p, int y, const int (&per_range)[2], int& local) {
+  if (p.n_ranges > 1 && y < per_range[1]) {
+    local = y;
+    return 1;
+  }
+  local = y - (p.n_ranges > 1 ? per_range[1] : 0);
+  return 0;
+}
 
 // Softmax-warp wait: once any wait of this thread gave up (`alive` false) later waits are
 // skipped, so the warp still runs its remaining iterations and every named barrier stays matched.
@@ -59,8 +74,12 @@ static cudaError_t launch_attention_simt(const __nv_bfloat16* qkv, int64_t ld_qk
 cudaError_t launch_attention(const __nv_bfloat16* qkv, int64_t ld_qkv, int64_t q_col, int64_t k_col, int64_t v_col,
                              int64_t B, int64_t S, int64_t H, int64_t hd, const int32_t* kv_len, int causal,
                              float scale, __nv_bfloat16* ctx, int64_t ld_ctx, cudaStream_t stream,
-                             int64_t q_begin = 0, int64_t q_count = -1) {
-  if (q_count < 0) q_count = S - q_begin;
+                             const int64_t* q_ranges = nullptr, int n_ranges = 0) {
+  const int64_t whole[2] = {0, S};
+  if (n_ranges == 0) {
+    q_ranges = whole;
+    n_ranges = 1;
+  }
   AttnParams p;
   p.ctx = ctx;
   p.ld_ctx = ld_ctx;
@@ -73,9 +92,14 @@ cudaError_t launch_attention(const __nv_bfloat16* qkv, int64_t ld_qkv, int64_t q
   p.v_col = static_cast<int>(v_col);
   p.causal = causal;
   p.scale_log2 = scale * 1.4426950408889634f;
-  p.q_tile0 = static_cast<int>(q_begin / 128);
-  p.q_end = static_cast<int>(q_begin + q_count);
-  p.n_q_tiles = static_cast<int>((q_count + 127) / 128);
+  p.n_ranges = n_ranges;
+  for (int r = 0; r < 2; ++r) {
+    const int64_t q_begin = r < n_ranges ? q_ranges[2 * r] : 0;
+    const int64_t q_count = r < n_ranges ? q_ranges[2 * r + 1] : 0;
+    p.q_tile0[r] = static_cast<int>(q_begin / 128);
+    p.q_end[r] = static_cast<int>(q_begin + q_count);
+    p.n_q_tiles[r] = static_cast<int>((q_count + 127) / 128);
+  }
   switch (hd) {
     case 8:
       return launch_attention_simt<8>(qkv, ld_qkv, p, stream);

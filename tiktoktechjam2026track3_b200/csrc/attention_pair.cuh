@@ -124,21 +124,25 @@ __global__ void __launch_bounds__(AttnPairCfg<HD>::kThreads, 1)
   const int lane = threadIdx.x & 31;
   const int b = blockIdx.x / p.H;
   const int h = blockIdx.x % p.H;
-  const int n_pairs = (p.n_q_tiles + 1) >> 1;
-  const int pair = n_pairs - 1 - static_cast<int>(blockIdx.y);  // heaviest causal pairs first
+  const int range_pairs[2] = {(p.n_q_tiles[0] + 1) >> 1, (p.n_q_tiles[1] + 1) >> 1};
+  int y_local;
+  const int rg = attn_range_of(p, static_cast<int>(blockIdx.y), range_pairs, y_local);
+  const int pair = range_pairs[rg] - 1 - y_local;  // heaviest causal pairs first
+  const int q_tile0 = p.q_tile0[rg];
+  const int q_end = p.q_end[rg];
   const int kv_len = p.kv_len != nullptr ? p.kv_len[b] : p.S;
   const int kv_tiles = (kv_len + 127) >> 7;
   int n_kv[2];
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
-    const int qt = p.q_tile0 + 2 * pair + t;  // absolute query tile
-    const bool live = 2 * pair + t < p.n_q_tiles && qt * 128 < kv_len;
+    const int qt = q_tile0 + 2 * pair + t;  // absolute query tile
+    const bool live = 2 * pair + t < p.n_q_tiles[rg] && qt * 128 < kv_len;
     n_kv[t] = live ? (p.causal ? min(qt + 1, kv_tiles) : kv_tiles) : 0;
   }
   const int n_total = max(n_kv[0], n_kv[1]);
   if (n_total == 0) return;  // uniform for the CTA: nothing allocated yet
   const int row_base = b * p.S;
-  const int q_row0 = row_base + (p.q_tile0 + 2 * pair) * 128;
+  const int q_row0 = row_base + (q_tile0 + 2 * pair) * 128;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -346,7 +350,7 @@ __global__ void __launch_bounds__(AttnPairCfg<HD>::kThreads, 1)
     const int grp = (warp - Cfg::kSoftmaxWarp0) >> 2;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
-    const int qt = p.q_tile0 + 2 * pair + grp;
+    const int qt = q_tile0 + 2 * pair + grp;
     const int query = qt * 128 + r;
     const int n = grp == 0 ? n_kv[0] : n_kv[1];
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
@@ -479,7 +483,7 @@ __global__ void __launch_bounds__(AttnPairCfg<HD>::kThreads, 1)
       for (int cc = 0; cc < HD / 32; ++cc) {
         float o[32];
         tmem_load_32cols(t_o + 32 * cc, o);
-        if (query < p.q_end) {
+        if (query < q_end) {
 #pragma unroll
           for (int k = 0; k < 4; ++k)
             dst[4 * cc + k] = make_uint4(pack_bf16x2(o[8 * k] * inv, o[8 * k + 1] * inv),
@@ -510,7 +514,7 @@ static cudaError_t launch_attention_pair(const CUtensorMap& tm, const AttnParams
                                     Cfg::kSmemBytes);
   });
   if (attr_err != cudaSuccess) return attr_err;
-  dim3 grid(p.B * p.H, (p.n_q_tiles + 1) / 2);
+  dim3 grid(p.B * p.H, (p.n_q_tiles[0] + 1) / 2 + (p.n_ranges > 1 ? (p.n_q_tiles[1] + 1) / 2 : 0));
   return launch_pdl(attention_pair_kernel<HD>, grid, dim3(Cfg::kThreads), Cfg::kSmemBytes, stream, tm, p);
 }
 

@@ -37,16 +37,21 @@ __global__ void __launch_bounds__(128) attention_simt_kernel(const __nv_bfloat16
 
   const int b = blockIdx.x / p.H;
   const int h = blockIdx.x % p.H;
-  const int q0 = p.q_tile0 * 128 + blockIdx.y * Cfg::kQPB;
+  const int range_blocks[2] = {(p.q_end[0] - p.q_tile0[0] * 128 + Cfg::kQPB - 1) / Cfg::kQPB,
+                               (p.q_end[1] - p.q_tile0[1] * 128 + Cfg::kQPB - 1) / Cfg::kQPB};
+  int y_local;
+  const int rg = attn_range_of(p, static_cast<int>(blockIdx.y), range_blocks, y_local);
+  const int q_end = p.q_end[rg];
+  const int q0 = p.q_tile0[rg] * 128 + y_local * Cfg::kQPB;
   const int kv_len = p.kv_len != nullptr ? p.kv_len[b] : p.S;
   const int qi = q0 + static_cast<int>(threadIdx.x) / Cfg::kTPQ;
   const int sub = static_cast<int>(threadIdx.x) % Cfg::kTPQ;
   const int d0 = sub * Cfg::kDPT;
   const int64_t row_base = static_cast<int64_t>(b) * p.S;
-  const bool live = qi < p.q_end;
+  const bool live = qi < q_end;
   const int limit = p.causal ? min(kv_len, qi + 1) : kv_len;
   // Keys the block needs: up to the last query's causal limit.
-  const int q_last = min(q0 + Cfg::kQPB, p.q_end) - 1;
+  const int q_last = min(q0 + Cfg::kQPB, q_end) - 1;
   const int block_keys = p.causal ? min(kv_len, q_last + 1) : kv_len;
 
   float q[Cfg::kDPT], o[Cfg::kDPT];
@@ -138,7 +143,9 @@ static cudaError_t launch_attention_simt(const __nv_bfloat16* qkv, int64_t ld_qk
     });
     if (attr_err != cudaSuccess) return attr_err;
   }
-  dim3 grid(p.B * p.H, (p.q_end - p.q_tile0 * 128 + Cfg::kQPB - 1) / Cfg::kQPB);
+  unsigned rows = 0;
+  for (int r = 0; r < p.n_ranges; ++r) rows += (p.q_end[r] - p.q_tile0[r] * 128 + Cfg::kQPB - 1) / Cfg::kQPB;
+  dim3 grid(p.B * p.H, rows);
   return launch_pdl(attention_simt_kernel<HD>, grid, dim3(Cfg::kThreads), Cfg::kSmemBytes, stream, qkv, ld_qkv, p);
 }
 

@@ -164,8 +164,8 @@ B2_API int b2_linear_fwd(const void* a, const void* w, const void* bias, int64_t
 
 B2_API int b2_attention_rows_fwd(const void* qkv, int64_t ld_qkv, int64_t q_col, int64_t k_col, int64_t v_col,
                                  int64_t batch, int64_t seq_len, int64_t num_heads, int64_t head_dim,
-                                 const int32_t* kv_len, int causal, float scale, int64_t q_begin, int64_t q_count,
-                                 void* ctx, int64_t ld_ctx, void* stream) {
+                                 const int32_t* kv_len, int causal, float scale, const int64_t* q_ranges,
+                                 int n_ranges, void* ctx, int64_t ld_ctx, void* stream) {
   if (qkv == nullptr || ctx == nullptr) return fail(1, "b2_attention_rows_fwd: null pointer argument");
   if (batch < 0 || seq_len < 0 || num_heads <= 0) return fail(1, "b2_attention_rows_fwd: invalid shape");
   const bool tensor_core = head_dim == 64 || head_dim == 128;
@@ -183,24 +183,35 @@ B2_API int b2_attention_rows_fwd(const void* qkv, int64_t ld_qkv, int64_t q_col,
   if (batch * seq_len > 0x7fffff00LL || batch * num_heads > 0x7fffffffLL || (seq_len + 127) / 128 > 65535)
     return fail(2, "b2_attention_rows_fwd: problem too large");
   if (!(scale > 0.f)) return fail(1, "b2_attention_rows_fwd: scale must be positive");
-  if (q_begin < 0 || q_count < 0 || q_begin + q_count > seq_len || q_begin % 128 != 0 ||
-      (q_count % 128 != 0 && q_begin + q_count != seq_len))
-    return fail(1, "b2_attention_rows_fwd: query rows [%lld, +%lld) must start on a multiple of 128 and end on one or at "
-                "seq_len", (long long)q_begin, (long long)q_count);
-  if (batch == 0 || seq_len == 0 || q_count == 0) return 0;
+  if (q_ranges == nullptr || n_ranges < 1 || n_ranges > 2)
+    return fail(1, "b2_attention_rows_fwd: 1 or 2 query ranges are required");
+  int64_t rows = 0;
+  for (int r = 0; r < n_ranges; ++r) {
+    const int64_t q_begin = q_ranges[2 * r], q_count = q_ranges[2 * r + 1];
+    if (q_begin < 0 || q_count <= 0 || q_begin + q_count > seq_len || q_begin % 128 != 0 ||
+        (q_count % 128 != 0 && q_begin + q_count != seq_len))
+      return fail(1, "b2_attention_rows_fwd: query rows [%lld, +%lld) must be non-empty, start on a multiple of 128 "
+                  "and end on one or at seq_len", (long long)q_begin, (long long)q_count);
+    if (r == 1 && q_begin < q_ranges[0] + q_ranges[1])
+      return fail(1, "b2_attention_rows_fwd: the second query range must start after the first one ends");
+    rows += q_count;
+  }
+  if (batch == 0 || seq_len == 0 || rows == 0) return 0;
   if (!is_sm100(nullptr)) return fail(2, "b2_attention_rows_fwd: needs an sm_100 (B200) device");
   return check_launch(launch_attention(static_cast<const __nv_bfloat16*>(qkv), ld_qkv, q_col, k_col, v_col, batch,
                                        seq_len, num_heads, head_dim, kv_len, causal, scale,
-                                       static_cast<__nv_bfloat16*>(ctx), ld_ctx, static_cast<cudaStream_t>(stream), q_begin,
-                                       q_count),
+                                       static_cast<__nv_bfloat16*>(ctx), ld_ctx, static_cast<cudaStream_t>(stream), q_ranges,
+                                       n_ranges),
                       "b2_attention_rows_fwd");
 }
 
 B2_API int b2_attention_fwd(const void* qkv, int64_t ld_qkv, int64_t q_col, int64_t k_col, int64_t v_col,
                             int64_t batch, int64_t seq_len, int64_t num_heads, int64_t head_dim, const int32_t* kv_len,
                             int causal, float scale, void* ctx, int64_t ld_ctx, void* stream) {
+  const int64_t whole[2] = {0, seq_len};
+  if (seq_len == 0 && batch >= 0 && num_heads > 0) return 0;
   const int rc = b2_attention_rows_fwd(qkv, ld_qkv, q_col, k_col, v_col, batch, seq_len, num_heads, head_dim, kv_len,
-                                       causal, scale, 0, seq_len < 0 ? 0 : seq_len, ctx, ld_ctx, stream);
+                                       causal, scale, whole, 1, ctx, ld_ctx, stream);
   if (rc != 0) {
     std::string msg = g_last_error;
     const std::string from = "b2_attention_rows_fwd";
@@ -260,11 +271,11 @@ B2_API int b2_linear_rs_fwd(const void* a, const void* w, const void* bias, int6
   if (n % 32 != 0 || k % 8 != 0 || ldo < n || ldo % 8 != 0)
     return fail(2, "b2_linear_rs_fwd: n %% 32, k %% 8, ldo >= n and ldo %% 8 are required");
   if ((tile_n & ~(kTilePair | 0xFFFF)) != 0) return fail(1, "b2_linear_rs_fwd: bad tile_n");
-  float* peers[kGemmMaxPeers] = {};
+  void* peers[kGemmMaxPeers] = {};
   for (int r = 0; r < world; ++r) {
     if (peer_resid[r] == nullptr || !aligned16(peer_resid[r]))
       return fail(2, "b2_linear_rs_fwd: residual of rank %d is null or not 16-byte aligned", r);
-    peers[r] = static_cast<float*>(peer_resid[r]);
+    peers[r] = peer_resid[r];
   }
   if (!aligned16(a) || !aligned16(w) || (bias && !aligned16(bias)))
     return fail(2, "b2_linear_rs_fwd: pointers must be 16-byte aligned");
@@ -299,4 +310,32 @@ B2_API int b2_layernorm_gather_fwd(const float* x, const void* gamma, const void
                                               static_cast<const __nv_bfloat16*>(beta), eps, dst, world, row_mask, rows,
                                               d_model, static_cast<cudaStream_t>(stream)),
                       "b2_layernorm_gather_fwd");
+}
+
+B2_API int b2_linear_bcast_fwd(const void* a, const void* w, const void* bias, int64_t m, int64_t n, int64_t k,
+                               void* const* peer_out, int world, int rank, int64_t col_begin, int64_t ldo, int tile_n,
+                               void* stream) {
+  if (a == nullptr || w == nullptr || peer_out == nullptr) return fail(1, "b2_linear_bcast_fwd: null pointer argument");
+  if (m < 0 || n <= 0 || k <= 0) return fail(1, "b2_linear_bcast_fwd: invalid shape");
+  if (world < 1 || world > kGemmMaxPeers || rank < 0 || rank >= world)
+    return fail(1, "b2_linear_bcast_fwd: rank %d / world %d invalid (world <= %d)", rank, world, kGemmMaxPeers);
+  if (n % 32 != 0 || k % 8 != 0 || ldo < n || ldo % 8 != 0)
+    return fail(2, "b2_linear_bcast_fwd: n %% 32, k %% 8, ldo >= n and ldo %% 8 are required");
+  if (col_begin < 0 || col_begin > n || col_begin % 32 != 0)
+    return fail(1, "b2_linear_bcast_fwd: col_begin must be a multiple of 32 in [0, n]");
+  if ((tile_n & ~(kTilePair | 0xFFFF)) != 0) return fail(1, "b2_linear_bcast_fwd: bad tile_n");
+  void* peers[kGemmMaxPeers] = {};
+  for (int r = 0; r < world; ++r) {
+    if (peer_out[r] == nullptr || !aligned16(peer_out[r]))
+      return fail(2, "b2_linear_bcast_fwd: output of rank %d is null or not 16-byte aligned", r);
+    peers[r] = peer_out[r];
+  }
+  if (!aligned16(a) || !aligned16(w) || (bias && !aligned16(bias)))
+    return fail(2, "b2_linear_bcast_fwd: pointers must be 16-byte aligned");
+  if (m == 0) return 0;
+  if (!is_sm100(nullptr)) return fail(2, "b2_linear_bcast_fwd: needs an sm_100 (B200) device");
+  return check_launch(launch_gemm(static_cast<const __nv_bfloat16*>(a), static_cast<const __nv_bfloat16*>(w),
+                                  static_cast<const __nv_bfloat16*>(bias), m, n, k, kEpiBiasPeers, peers[rank], ldo,
+                                  nullptr, tile_n, static_cast<cudaStream_t>(stream), peers, world, rank, 0, col_begin),
+                      "b2_linear_bcast_fwd");
 }

@@ -43,6 +43,7 @@ enum GemmEpilogue : int {
   kEpiStoreF32 = 4,
   kEpiRsResidual = 5,
   kEpiRsResidualZero = 6,
+  kEpiBiasPeers = 7,
 };
 
 constexpr int kGemmMaxPeers = 8;
@@ -55,8 +56,9 @@ struct GemmParams {
   int M, N, K;
   int m_blocks, n_blocks, k_blocks;
   // kEpiRs*: every rank's residual base (as mapped here); row r belongs to rank r / rows_per_rank.
-  float* peer_out[kGemmMaxPeers];
-  int rows_per_rank, world, rank;
+  // kEpiBiasPeers: every rank's output base; columns >= peer_col go to every rank's copy.
+  void* peer_out[kGemmMaxPeers];
+  int rows_per_rank, world, rank, peer_col;
 };
 
 constexpr int kGemmBM = 128;
@@ -156,7 +158,7 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmParams& p, int row
     for (int i = 0; i < 8; ++i) {
       if (!live[i]) continue;
       const int64_t off = static_cast<int64_t>(row0 + i * 4 + (lane >> 3)) * p.ldo + col;
-      if constexpr (EPI == kEpiBias || EPI == kEpiBiasGelu) {
+      if constexpr (EPI == kEpiBias || EPI == kEpiBiasGelu || EPI == kEpiBiasPeers) {
         float4 w = v[i];
         if constexpr (EPI == kEpiBiasGelu) {
           w.x = gelu_erf(bf16_round(w.x));
@@ -164,14 +166,20 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmParams& p, int row
           w.z = gelu_erf(bf16_round(w.z));
           w.w = gelu_erf(bf16_round(w.w));
         }
-        *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.out) + off) =
-            make_uint2(pack_bf16x2(w.x, w.y), pack_bf16x2(w.z, w.w));
+        const uint2 packed = make_uint2(pack_bf16x2(w.x, w.y), pack_bf16x2(w.z, w.w));
+        *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.out) + off) = packed;
+        if constexpr (EPI == kEpiBiasPeers) {
+          if (col0 >= p.peer_col) {  // warp-uniform: a chunk's 32 columns are on one side
+            for (int r = 0; r < p.world; ++r)
+              if (r != p.rank) *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.peer_out[r]) + off) = packed;
+          }
+        }
       } else if constexpr (EPI == kEpiStoreF32) {
         *reinterpret_cast<float4*>(static_cast<float*>(p.out) + off) = v[i];
       } else {  // reduce-scatter: the row owner's copy
         const int row = row0 + i * 4 + (lane >> 3);
         const int owner = min(row / p.rows_per_rank, p.world - 1);
-        float* dst = p.peer_out[owner] + off;
+        float* dst = static_cast<float*>(p.peer_out[owner]) + off;
         if (keep[i])
           red_add_v4_sys(dst, v[i].x, v[i].y, v[i].z, v[i].w);
         else if (EPI == kEpiRsResidualZero && owner == p.rank)
@@ -351,7 +359,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_before_sync();
       mbar_arrive(&acc_empty[acc]);
     }
-    if constexpr (is_rs_epi<EPI>()) fence_acq_rel_sys();
+    if constexpr (is_rs_epi<EPI>() || EPI == kEpiBiasPeers) fence_acq_rel_sys();
   }
 
   __syncthreads();
@@ -535,7 +543,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       tc_fence_before_sync();
       mbar_arrive_cluster(acc ? acc_empty_leader1 : acc_empty_leader0);
     }
-    if constexpr (is_rs_epi<EPI>()) fence_acq_rel_sys();
+    if constexpr (is_rs_epi<EPI>() || EPI == kEpiBiasPeers) fence_acq_rel_sys();
   }
 
   if (*abort_flag && threadIdx.x == 0) {
@@ -611,6 +619,8 @@ static cudaError_t dispatch_epi2(int epi, const CUtensorMap& ta, const CUtensorM
       return launch_gemm2_t<BN, kEpiRsResidual>(ta, tb, p, grid, stream);
     case kEpiRsResidualZero:
       return launch_gemm2_t<BN, kEpiRsResidualZero>(ta, tb, p, grid, stream);
+    case kEpiBiasPeers:
+      return launch_gemm2_t<BN, kEpiBiasPeers>(ta, tb, p, grid, stream);
     default:
       return cudaErrorInvalidValue;
   }
@@ -634,6 +644,8 @@ static cudaError_t dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMa
       return launch_gemm_t<BN, kEpiRsResidual>(ta, tb, p, grid, stream);
     case kEpiRsResidualZero:
       return launch_gemm_t<BN, kEpiRsResidualZero>(ta, tb, p, grid, stream);
+    case kEpiBiasPeers:
+      return launch_gemm_t<BN, kEpiBiasPeers>(ta, tb, p, grid, stream);
     default:
       return cudaErrorInvalidValue;
   }
@@ -683,8 +695,8 @@ int gemm_pick_tile(int M, int N, int K, int sm_count) {
 
 cudaError_t launch_gemm(const __nv_bfloat16* A, const __nv_bfloat16* W, const __nv_bfloat16* bias, int64_t M,
                         int64_t N, int64_t K, int epi, void* out, int64_t ldo, const uint8_t* row_mask, int tile,
-                        cudaStream_t stream, float* const* peer_out = nullptr, int world = 1, int rank = 0,
-                        int64_t rows_per_rank = 0) {
+                        cudaStream_t stream, void* const* peer_out = nullptr, int world = 1, int rank = 0,
+                        int64_t rows_per_rank = 0, int64_t peer_col = 0) {
   int dev = 0;
   cudaGetDevice(&dev);
   const int sms = device_sm_count(dev);
@@ -702,6 +714,7 @@ cudaError_t launch_gemm(const __nv_bfloat16* A, const __nv_bfloat16* W, const __
   p.world = world;
   p.rank = rank;
   p.rows_per_rank = static_cast<int>(rows_per_rank);
+  p.peer_col = static_cast<int>(peer_col);
   p.out = out;
   p.ldo = ldo;
   p.bias = bias;

@@ -76,7 +76,8 @@ class _PackedBlock:
 
 
 def _param_key(t: torch.Tensor) -> Tuple[int, int, torch.device, torch.dtype]:
-    return (t.data_ptr(), t._version, t.device, t.dtype)
+    # Inference tensors (a model built under torch.inference_mode) carry no version counter.
+    return (t.data_ptr(), 0 if t.is_inference() else t._version, t.device, t.dtype)
 
 
 class MaskLengths:

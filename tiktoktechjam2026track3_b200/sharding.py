@@ -314,3 +314,178 @@ class TensorParallelTransformer:
     def close(self) -> None:
         """Drops the symmetric-memory buffers (call on every rank before destroying the group)."""
         self._symm_rs = None
+
+
+def cp_chunks(seq_len: int, world: int, rank: int) -> Tuple[int, Tuple[int, int]]:
+    """Context-parallel split of a sequence into 2 * world chunks (zigzag): rank r owns chunks r and
+    2 * world - 1 - r, so every rank gets one early and one late chunk and the causal work is
+    balanced. Returns (chunk rows, (first chunk index, second chunk index))."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"invalid rank {rank} of world {world}")
+    if seq_len % (2 * world * 128):
+        raise ValueError(f"seq_len={seq_len} must be a multiple of 2 x {world} ranks x 128 for context parallelism")
+    return seq_len // (2 * world), (rank, 2 * world - 1 - rank)
+
+
+class ContextParallelTransformer:
+    """Forward pass of the stack with each sequence's tokens split over a process group (context
+    parallelism, for single long sequences): every rank holds all weights and runs the LayerNorms
+    and GEMMs on its own token rows, and the attention of its query rows against every key.
+    The K/V exchange is fused into the QKV GEMM: its epilogue stores the K and V columns of the
+    rank's rows into every rank's full-length QKV buffer over NVLink (b2_linear_bcast_fwd).
+
+    Token rows of each sequence are split into 2n chunks, rank r owning chunks r and 2n-1-r (zigzag:
+    equal causal work per rank). Per layer a rank computes Q/K/V for its rows into its full-length
+    [B*S, 3D] QKV buffer (torch symmetric memory), K and V also into every other rank's buffer —
+    the all-gather of K and V, (n-1)/n of 2 bf16 [T, D] per GPU per layer, no reduction anywhere —
+    then runs `b2_attention_rows_fwd` over its two query chunks in one launch
+    (the later, heavier chunk's tiles first). Two flag
+    barriers per layer (b2_peer_barrier): peers are done reading their QKV buffers before they are
+    written, and every chunk has landed before attention reads it. The output is gathered to every
+    rank the same way. Built from the full model's state dict (reference key names).
+    """
+
+    def __init__(self, config, state: Dict[str, torch.Tensor], device: torch.device, group=None) -> None:
+        import torch.distributed as dist
+
+        from .models import UserOptimizedTransformer
+
+        self.config = config_from(config)
+        self.config.validate()
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.device = device
+        with torch.inference_mode(False):  # ordinary parameters even when built under inference mode
+            model = UserOptimizedTransformer(self.config)
+            model.load_state_dict(state, strict=True)
+            self.model = model.to(device=device, dtype=torch.bfloat16).eval()
+        self.collective = "cp"
+        self._mask_lengths = MaskLengths()
+        self._launch_log: Optional[list] = None
+        self._buf: Optional[dict] = None
+
+    record_launches = TensorParallelTransformer.record_launches
+    take_launch_log = TensorParallelTransformer.take_launch_log
+    _timed = TensorParallelTransformer._timed
+
+    def _buffers(self, batch: int, seq_len: int) -> dict:
+        if self._buf is not None and self._buf["shape"] == (batch, seq_len):
+            return self._buf
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self._buf = None
+        d = self.config.d_model
+        tokens = batch * seq_len
+        n_qkv, n_out = tokens * 3 * d, tokens * d
+        buf = symm_mem.empty(n_qkv + n_out + 64, dtype=torch.bfloat16, device=self.device)
+        buf[n_qkv + n_out:].zero_()
+        group = self.group if self.group is not None else dist.group.WORLD
+        handle = symm_mem.rendezvous(buf, group)
+        total = n_qkv + n_out + 64
+        peers = [handle.get_buffer(r, (total,), torch.bfloat16) for r in range(self.world)]
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # every pad is zero before any rank signals
+        chunk, mine = cp_chunks(seq_len, self.world, self.rank)
+        pieces = [(b * seq_len + c * chunk, chunk) for b in range(batch) for c in mine]  # (first row, rows)
+        self._buf = {
+            "shape": (batch, seq_len), "buf": buf, "handle": handle, "chunk": chunk, "mine": mine,
+            "pieces": pieces,
+            "qkv": [p[:n_qkv].view(tokens, 3 * d) for p in peers],  # every rank's QKV buffer
+            "out": [p[n_qkv:n_qkv + n_out].view(tokens, d) for p in peers],
+            "pads": [int(x) + (n_qkv + n_out) * 2 for x in handle.buffer_ptrs],
+            "ctx": torch.empty(tokens, d, device=self.device, dtype=torch.bfloat16),
+        }
+        return self._buf
+
+    def _barrier(self, pads: List[int], channel: int) -> None:
+        _capi.peer_barrier(pads, self.rank, channel, self.device)
+
+    def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+        cfg = self.config
+        if not x.is_cuda or x.dtype != torch.bfloat16:
+            raise RuntimeError("ContextParallelTransformer needs a bf16 CUDA input")
+        batch, seq_len, d = x.shape
+        if valid_token_mask is not None and valid_token_mask.device != x.device:
+            raise ValueError("valid_token_mask must be on x's device")
+        kv_len, row_mask = self._mask_lengths(valid_token_mask, batch, seq_len)
+        sb = self._buffers(batch, seq_len)
+        pieces, chunk, pads = sb["pieces"], sb["chunk"], sb["pads"]
+        qkv_all, out_all, ctx = sb["qkv"], sb["out"], sb["ctx"]
+        qkv = qkv_all[self.rank]
+        h, hd = cfg.num_heads, cfg.head_dim
+        t_loc = len(pieces) * chunk
+        dev = x.device
+        x2 = x.contiguous().view(batch * seq_len, d)
+        x_loc = torch.cat([x2[r0:r0 + n] for r0, n in pieces], 0)
+        mask_loc = torch.cat([row_mask[r0:r0 + n] for r0, n in pieces], 0) if row_mask is not None else None
+        resid = torch.empty(t_loc, d, device=dev, dtype=torch.float32)
+        ln = torch.empty(t_loc, d, device=dev, dtype=torch.bfloat16)
+        hidden = torch.empty(t_loc, cfg.ffn_dim, device=dev, dtype=torch.bfloat16)
+        out_loc = torch.empty(t_loc, d, device=dev, dtype=torch.bfloat16)
+        packed = self.model.packed_weights()
+        t = self._timed
+        ch = 0
+
+        def barrier():
+            nonlocal ch
+            t("barrier", self._barrier, pads, ch)
+            ch = (ch + 1) % 4
+
+        def local(buf, k):  # rows of piece k in a local [t_loc, *] buffer
+            return buf[k * chunk:(k + 1) * chunk]
+
+        def rows(buf, k):  # rows of piece k at their absolute positions in a [B*S, *] buffer
+            r0, n = pieces[k]
+            return buf[r0:r0 + n]
+
+        def broadcast(bufs, src):  # this rank's pieces of src into every other rank's copy
+            for r in range(self.world):
+                if r != self.rank:
+                    for k in range(len(pieces)):
+                        rows(bufs[r], k).copy_(rows(src, k), non_blocking=True)
+
+        pb0 = packed[0]
+        t("layernorm", _capi.layernorm, x_loc, pb0.ln1_w, pb0.ln1_b, pb0.ln1_eps, ln, resid_out=resid)
+        for i, pb in enumerate(packed):
+            if i > 0:
+                t("layernorm", _capi.layernorm, resid, pb.ln1_w, pb.ln1_b, pb.ln1_eps, ln)
+            barrier()  # peers are done reading their QKV buffers (previous layer's attention)
+            for k in range(len(pieces)):  # K and V columns also stored into every peer's buffer
+                row0 = pieces[k][0]
+                t("gemm_qkv", _capi.linear_bcast, local(ln, k), pb.w_qkv, pb.b_qkv,
+                  [q.data_ptr() + row0 * 3 * d * 2 for q in qkv_all], self.rank, d, 3 * d)
+            barrier()  # every rank's rows have landed in every copy
+            t("attention", _capi.attention, qkv, batch, seq_len, h, hd, 0, d, 2 * d, kv_len, cfg.causal, hd**-0.5,
+              ctx, q_rows=[(c * chunk, chunk) for c in sb["mine"]])
+            for k in range(len(pieces)):
+                t("gemm_out", _capi.linear, rows(ctx, k), pb.w_o, pb.b_o, _capi.EPI_RESIDUAL, local(resid, k),
+                  local(mask_loc, k) if mask_loc is not None else None)
+            t("layernorm", _capi.layernorm, resid, pb.ln2_w, pb.ln2_b, pb.ln2_eps, ln)
+            t("gemm_ffn_in", _capi.linear, ln, pb.w_1, pb.b_1, _capi.EPI_BIAS_GELU, hidden)
+            t("gemm_ffn_out", _capi.linear, hidden, pb.w_2, pb.b_2, _capi.EPI_RESIDUAL_ZERO, resid, mask_loc)
+        fn = self.model.final_norm
+        t("layernorm", _capi.layernorm, resid, fn.weight, fn.bias, float(fn.eps), out_loc, row_mask=mask_loc)
+        out_mine = out_all[self.rank]
+        for k in range(len(pieces)):
+            rows(out_mine, k).copy_(local(out_loc, k), non_blocking=True)
+        barrier()  # peers are done with their previous output copies
+        t("allgather", broadcast, out_all, out_mine)
+        barrier()
+        out = out_mine.view(batch, seq_len, d).clone()
+        self._mask_lengths.raise_if_invalid()
+        return out
+
+    __call__ = forward
+
+    def launches_per_forward(self, num_layers: int) -> int:
+        """Kernels of this library per forward (copies not counted): per layer one QKV and one
+        out_proj GEMM per piece (2 pieces per sequence), 1 attention launch, 2 barriers,
+        LayerNorm x 2, ffn_in, ffn_out; then the final LayerNorm and 2 barriers."""
+        p = 2 * self.config.batch_size
+        return num_layers * (2 * p + 7) + 3
+
+    def close(self) -> None:
+        """Drops the symmetric-memory buffers (call on every rank before destroying the group)."""
+        self._buf = None
