@@ -68,7 +68,7 @@ def parse_args(argv=None):
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--workload", default="c2", choices=sorted(BASELINE_CONFIGS))
     p.add_argument("--impl", default="ours", choices=("ours", "reference"))
-    p.add_argument("--split", default="tp", choices=("tp", "cp"),
+    p.add_argument("--split", default="cp", choices=("tp", "cp"),
                    help="batch smaller than the GPU count: head/FFN tensor parallel (tp) or context parallel (cp)")
     p.add_argument("--collective", default="auto", choices=("auto", "rs", "nccl"),
                    help="tensor-parallel reduction: reduce-scatter in the GEMMs + all-gather in the LayerNorm over "
@@ -318,8 +318,9 @@ def main() -> None:
     cfg, pad = workload_config(args.workload)
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.manual_seed(0)
-    # A batch smaller than the GPU count (c4: one sequence) runs tensor parallel over all ranks
-    # (strong scaling); everything else gives each rank its own batch shard (weak scaling).
+    # A batch smaller than the GPU count (c4: one sequence) is split over all ranks — context
+    # parallel by default, tensor parallel with --split tp — (strong scaling); everything else
+    # gives each rank its own batch shard (weak scaling).
     tensor_parallel = world > 1 and cfg.batch_size < world
     if tensor_parallel:
         from tiktoktechjam2026track3_b200.sharding import ContextParallelTransformer, TensorParallelTransformer
