@@ -205,6 +205,82 @@ def test_reduce_scatter_plan_matches_full_model_over_gloo(pad, world):
     assert max(errs.values()) < 1e-4, errs
 
 
+def _cp_rank(rank, world, port, cfg, pad, result_queue):
+    """The context-parallel plan's step sequence (ContextParallelTransformer.forward) with fp32
+    torch ops: LayerNorms and GEMMs on this rank's zigzag chunks only, K/V rows all-gathered, the
+    attention of this rank's query rows against every key (absolute causal positions)."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        state = oracle.build_reference_state(cfg, 0)
+        x, mask = oracle.generate_random_case(cfg, torch.device("cpu"), torch.float32, 3, pad)
+        b, s, d = x.shape
+        h, hd = cfg.num_heads, cfg.d_model // cfg.num_heads
+        chunk, mine = cp_chunks(s, world, rank)
+        idx = torch.cat([torch.arange(bb * s + c * chunk, bb * s + (c + 1) * chunk) for bb in range(b) for c in mine])
+
+        def lin(t, name):
+            return t @ state[f"{name}.weight"].T + state[f"{name}.bias"]
+
+        def ln(t, name):
+            return F.layer_norm(t, (d,), state[f"{name}.weight"], state[f"{name}.bias"], 1e-5)
+
+        m_loc = mask.reshape(-1)[idx].reshape(-1, 1)
+        resid = x.reshape(-1, d)[idx].clone()
+        key_pos = torch.arange(s)
+        for i in range(cfg.num_layers):
+            p = f"layers.{i}"
+            y = ln(resid, f"{p}.norm1")
+            q_loc = lin(y, f"{p}.attention.q_proj")
+            kv_loc = torch.cat([lin(y, f"{p}.attention.k_proj"), lin(y, f"{p}.attention.v_proj")], 1)
+            gathered = [torch.zeros_like(kv_loc) for _ in range(world)]
+            dist.all_gather(gathered, kv_loc)  # every rank's K/V rows
+            kv = torch.zeros(b * s, 2 * d)
+            for r in range(world):
+                ch_r, mine_r = cp_chunks(s, world, r)
+                idx_r = torch.cat([torch.arange(bb * s + c * ch_r, bb * s + (c + 1) * ch_r)
+                                   for bb in range(b) for c in mine_r])
+                kv[idx_r] = gathered[r]
+            k = kv[:, :d].view(b, s, h, hd).transpose(1, 2)
+            v = kv[:, d:].view(b, s, h, hd).transpose(1, 2)
+            ctx = torch.zeros(b * s, d)
+            qpos = idx % s
+            qb = idx // s
+            qh = q_loc.view(-1, h, hd)
+            for n_row in range(idx.numel()):  # one query row at a time, absolute causal position
+                bb, qq = int(qb[n_row]), int(qpos[n_row])
+                sc = torch.einsum("hd,hkd->hk", qh[n_row], k[bb]) * hd**-0.5
+                hidden = key_pos > qq if cfg.causal else torch.zeros(s, dtype=torch.bool)
+                hidden = hidden | ~mask[bb]
+                sc = sc.masked_fill(hidden[None], float("-inf"))
+                ctx[n_row] = torch.einsum("hk,hkd->hd", torch.softmax(sc, -1), v[bb]).reshape(-1)
+            a = lin(ctx[: idx.numel()], f"{p}.attention.out_proj")
+            resid = torch.where(m_loc, resid + a, resid)
+            f = lin(F.gelu(lin(ln(resid, f"{p}.norm2"), f"{p}.ffn_in")), f"{p}.ffn_out")
+            resid = torch.where(m_loc, resid + f, torch.zeros_like(resid))
+        out_loc = torch.where(m_loc, ln(resid, "final_norm"), 0.0)
+        ref = oracle.forward(state, cfg, x, mask).reshape(-1, d)[idx]
+        result_queue.put((rank, float((out_loc - ref).abs().max())))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("pad,world", [(0.0, 2), (0.3, 2)])
+def test_context_parallel_plan_matches_full_model_over_gloo(pad, world):
+    cfg = TransformerConfig(2, 1024, 128, 2, 256, 2, True)  # chunks of 256 tokens
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_cp_rank, args=(r, world, port, cfg, pad, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    errs = dict(q.get(timeout=5) for _ in range(world))
+    assert max(errs.values()) < 1e-4, errs
+
+
 def _failing_rank(rank, world, port):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     from datetime import timedelta
