@@ -57,8 +57,8 @@ L2_FLUSH_BYTES = 256 << 20
 LONG_STEP_MS = 50.0
 # DRAM bytes (read + write) per launch of the dominant kernel class, averaged over the class's
 # launches in one forward, from an ncu capture of this bench (profiles/launches_bench_c2.md):
-# key = (workload, tensor-parallel ranks, kernel class).
-DRAM_BYTES_PER_LAUNCH = {("c2", 1, "gemm_tc_kernel"): 19221899.5}
+# key = (workload, tensor-parallel ranks, kernel class, LayerNorm fused into the residual GEMMs).
+DRAM_BYTES_PER_LAUNCH = {("c2", 1, "gemm_tc_kernel", False): 19221899.5}
 
 
 def parse_args(argv=None):
@@ -73,6 +73,9 @@ def parse_args(argv=None):
     p.add_argument("--collective", default="auto", choices=("auto", "rs", "nccl"),
                    help="tensor-parallel reduction: reduce-scatter in the GEMMs + all-gather in the LayerNorm over "
                         "NVLink (rs), or NCCL all-reduce")
+    p.add_argument("--fuse-ln", default="auto", choices=("auto", "on", "off"),
+                   help="LayerNorm inside the out_proj / ffn_out GEMM epilogues (auto: where the fused launch keeps "
+                        "the plain GEMM's one-CTA tiles)")
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
     p.add_argument("--cpu-seconds", type=float, default=15.0, help="target CPU time of the CPU baseline sample")
     return p.parse_args(argv)
@@ -116,10 +119,12 @@ def attention_flops(cfg: TransformerConfig, lengths) -> float:
     return cfg.num_layers * 4.0 * cfg.d_model * pairs
 
 
-def layernorm_bytes(cfg: TransformerConfig) -> float:
+def layernorm_bytes(cfg: TransformerConfig, fused: bool = False) -> float:
+    """Bytes of the LayerNorm launches: the first norm reads bf16 x and writes the fp32 residual + bf16
+    (8 B/elt); each other norm reads fp32 and writes bf16 (6 B/elt) — 2L of them, or only the final
+    norm when norm2 / norm1 run inside the residual GEMMs (their work is then part of those launches)."""
     t, d, layers = cfg.batch_size * cfg.seq_len, cfg.d_model, cfg.num_layers
-    # first norm reads bf16 x and writes fp32 residual + bf16 (8 B/elt); the other 2L reads fp32, writes bf16 (6 B)
-    return t * d * (8.0 + 6.0 * (2 * layers))
+    return t * d * (8.0 + 6.0 * (1 if fused else 2 * layers))
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -334,7 +339,9 @@ def main() -> None:
         x, mask = generate_random_case(cfg, device, torch.bfloat16, 100000, pad)
     else:
         model = UserOptimizedTransformer(cfg).to(device=device, dtype=torch.bfloat16).eval()
+        model.fuse_layernorm = {"auto": "auto", "on": True, "off": False}[args.fuse_ln]
         x, mask = generate_random_case(cfg, device, torch.bfloat16, 100000 + rank, pad)
+    ln_fused = (not tensor_parallel) and model.layernorm_fused(cfg.batch_size * cfg.seq_len)
     lengths = mask.sum(1).tolist() if pad > 0 else None
     use_mask = mask if pad > 0 else mask  # the harness always passes a mask; all-true masks are elided
     flush = torch.empty(L2_FLUSH_BYTES // 4, device=device, dtype=torch.float32)
@@ -436,7 +443,7 @@ def main() -> None:
                            "launches": sum(v for k, v in kind_n.items() if k.startswith("gemm")) // reps},
         "attention_pair_kernel": {"ms": kind_ms.get("attention", 0.0), "work": attn, "bound": "tensor",
                                 "launches": kind_n.get("attention", 0) // reps},
-        "layernorm_vec_kernel": {"ms": kind_ms.get("layernorm", 0.0), "work": layernorm_bytes(cfg), "bound": "hbm",
+        "layernorm_vec_kernel": {"ms": kind_ms.get("layernorm", 0.0), "work": layernorm_bytes(cfg, ln_fused), "bound": "hbm",
                                  "launches": kind_n.get("layernorm", 0) // reps},
     }
     kernels = {}
@@ -463,7 +470,7 @@ def main() -> None:
         "peak_source": f"{peak_src} ({tensor_peak_name if classes[dominant]['bound'] == 'tensor' else 'HBM copy'})",
         "unit": dk["unit"],
         "frac": dk["frac"],
-        "traffic": DRAM_BYTES_PER_LAUNCH.get((args.workload, world if tensor_parallel else 1, dominant)),
+        "traffic": DRAM_BYTES_PER_LAUNCH.get((args.workload, world if tensor_parallel else 1, dominant, ln_fused)),
         "work_per_launch": classes[dominant]["work"] / max(1, classes[dominant]["launches"]),
     }
     total_flops = gemm_total + attn  # per rank
@@ -511,6 +518,8 @@ def main() -> None:
                 "l2": "flushed (256 MiB write) before every timed step",
                 "launches": (f"eager launches ({model.collective})" if tensor_parallel else
                              "first/final LayerNorm eager, the block launches replayed from a CUDA graph"),
+                "layernorm": ("norm2 and the next block's norm1 in the out_proj / ffn_out GEMM epilogues "
+                              "(clusters spanning each row)") if ln_fused else "separate LayerNorm launches",
             },
             "roofline": roofline,
             "kernels": kernels,
@@ -523,7 +532,7 @@ def main() -> None:
             "e2e": {"value": tokens_per_step / (e2e_per_step / 1e3), "unit": UNIT, "ms_per_step": e2e_per_step,
                     "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world},
             "gpu_launches": args.steps * (model.launches_per_forward(cfg.num_layers) if tensor_parallel else
-                                          UserOptimizedTransformer.launches_per_forward(cfg.num_layers)),
+                                          UserOptimizedTransformer.launches_per_forward(cfg.num_layers, ln_fused)),
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)

@@ -98,6 +98,33 @@ int b2_linear_fwd(const void* a, const void* w, const void* bias, int64_t m, int
                   void* out, int64_t ldo, const uint8_t* row_mask, int tile_n, void* stream);
 
 /*
+ * A residual GEMM and the LayerNorm after it in one launch: resid = mask ? resid + A W^T + bias :
+ * (zero_masked_rows ? 0 : resid), then ln_out = LayerNorm(resid) with gamma, beta, eps (biased
+ * variance, fp32 statistics, bf16 out; every row normalised, masked ones included, as nn.LayerNorm
+ * does). Replaces out_proj + residual add + norm2 (models.py:76-79, 733, 723) and ffn_out +
+ * residual add + masked_fill + the next block's norm1 (:734-737, 721). A cluster of n / tile_n
+ * CTAs computes each 128-row stripe, and the CTAs exchange row sums through distributed shared
+ * memory, so the residual is read and written once and the LayerNorm needs no launch of its own.
+ *   a [m, k] bf16; w [n, k] bf16; bias [n] bf16 or NULL; resid [m, n] fp32 (in place);
+ *   row_mask [m] uint8 or NULL; gamma, beta [n] bf16; ln_out [m, n] bf16
+ * Requires n % 32 == 0 and a plan (b2_linear_ln_plan) for n: n <= 256, or n = tile_n x c with
+ * tile_n in {128, 192, 256} and c <= 8; k % 8 == 0; 16-byte aligned pointers; an sm_100 device.
+ */
+int b2_linear_ln_fwd(const void* a, const void* w, const void* bias, int64_t m, int64_t n, int64_t k,
+                     int zero_masked_rows, float* resid, const uint8_t* row_mask, const void* gamma, const void* beta,
+                     float eps, void* ln_out, void* stream);
+
+/*
+ * The tile b2_linear_ln_fwd uses for n output columns (no device work): returns 0 and sets *tile_n
+ * and *cluster (CTAs per 128-row stripe; n <= 256: one CTA, else a power-of-two cluster first,
+ * then the widest tile), and *recommended = 1 where the fused launch is expected to beat
+ * b2_linear_fwd + b2_layernorm_fwd. The plan depends on n only, so a row's output never depends on
+ * m (batch shards reproduce the full batch bit for bit). Returns 2 when n has no plan. m and k are
+ * validated only; sm_count is unused (kept for the signature).
+ */
+int b2_linear_ln_plan(int64_t m, int64_t n, int64_t k, int sm_count, int* tile_n, int* cluster, int* recommended);
+
+/*
  * Multi-head self-attention core (BaselineSelfAttention.forward, models.py:55-75) as one
  * flash-style tcgen05 kernel: scores = q k^T * scale, causal (key > query) and/or padding
  * (key >= kv_len[b]) masked to -inf, fp32 softmax, context = p v written as bf16 to

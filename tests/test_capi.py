@@ -68,3 +68,27 @@ def test_layernorm_rejects_bad_arguments(lib):
     assert lib.b2_layernorm_fwd(None, 0, p, p, 1e-5, p, None, None, 4, 8, None) == 1
     assert lib.b2_layernorm_fwd(p, 0, p, p, 0.0, p, None, None, 4, 8, None) == 1
     assert lib.b2_layernorm_fwd(p, 0, p, p, 1e-5, p, None, None, 0, 8, None) == 0  # empty is a no-op
+
+
+def test_linear_ln_plan_depends_on_n_only(lib):
+    for m in (1, 4096, 100000):
+        assert _capi.linear_ln_plan(m, 768, 768, sm_count=148) == (192, 4, True)
+    assert _capi.linear_ln_plan(4096, 1024, 4096, sm_count=148) == (256, 4, False)
+    assert _capi.linear_ln_plan(4096, 2048, 8192, sm_count=148) == (256, 8, False)
+    assert _capi.linear_ln_plan(64, 96, 64, sm_count=148) == (128, 1, True)
+    assert _capi.linear_ln_plan(64, 640, 64, sm_count=148) == (128, 5, True)
+    assert _capi.linear_ln_plan(64, 2560, 64, sm_count=148) is None  # 10 CTAs per row
+    assert _capi.linear_ln_plan(64, 48, 64, sm_count=148) is None
+
+
+def test_linear_ln_rejects_bad_arguments(lib):
+    p = ctypes.c_void_p(16)
+    f = lib.b2_linear_ln_fwd
+    assert f(None, p, p, 128, 768, 768, 0, p, None, p, p, 1e-5, p, None) == 1
+    assert f(p, p, p, 128, 768, 768, 0, p, None, p, p, 0.0, p, None) == 1
+    assert f(p, p, p, 128, 2560, 768, 0, p, None, p, p, 1e-5, p, None) == 2
+    assert b"plan" in lib.b2_last_error()
+    assert f(p, p, p, 128, 768, 60, 0, p, None, p, p, 1e-5, p, None) == 2
+    assert f(ctypes.c_void_p(8), p, p, 128, 768, 768, 0, p, None, p, p, 1e-5, p, None) == 2
+    assert b"aligned" in lib.b2_last_error()
+    assert f(p, p, p, 0, 768, 768, 0, p, None, p, p, 1e-5, p, None) == 0  # empty is a no-op

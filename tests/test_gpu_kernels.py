@@ -324,3 +324,65 @@ def test_add_layernorm(d, flags):
     if flags & 2:
         expect_y = torch.where(keep, expect_y, torch.zeros_like(expect_y))
     torch.testing.assert_close(y.float(), expect_y, atol=1e-2, rtol=8e-3)
+
+
+# ---------------------------------------------------------------------------------- GEMM + residual + LayerNorm
+LN_SHAPES = [  # (m, n, k): clusters of 1, 2, 4 and 8 CTAs, ragged m, n below one tile
+    (1000, 768, 768),    # C2 out_proj: 4 x 192
+    (4096, 768, 3072),   # C2 ffn_out
+    (777, 1024, 1024),   # 4 x 256 (3-deep ring)
+    (300, 2048, 512),    # 8 x 256
+    (513, 384, 256),     # 2 x 192
+    (256, 256, 256),     # one CTA, 256 wide
+    (130, 96, 64),       # one 128-wide tile holding 96 columns
+    (64, 32, 128),       # 32 columns
+]
+
+
+@pytest.mark.parametrize("m,n,k", LN_SHAPES)
+@pytest.mark.parametrize("zero", [False, True])
+def test_gemm_residual_layernorm(m, n, k, zero):
+    """b2_linear_ln_fwd: the residual is bit-identical to the plain residual GEMM with the same tile;
+    the LayerNorm output matches the separate LayerNorm kernel on that residual to within one bf16
+    ulp (the row statistics are summed in another order) and fp32 F.layer_norm within the usual
+    LayerNorm tolerance."""
+    a, w, bias, _ = _gemm_inputs(m, n, k, 7)
+    g = _gen(8)
+    resid0 = torch.randn(m, n, device="cuda", generator=g) * 2 + 0.3
+    mask = (torch.rand(m, device="cuda", generator=g) > 0.25).to(torch.uint8)
+    gamma = (torch.randn(n, device="cuda", generator=g) * 0.2 + 1).bfloat16()
+    beta = (torch.randn(n, device="cuda", generator=g) * 0.1).bfloat16()
+    tile, cluster, _ = _capi.linear_ln_plan(m, n, k)
+    assert 1 <= cluster <= 8 and (cluster == 1 or tile * cluster == n)
+    resid = resid0.clone()
+    y = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    _capi.linear_ln(a, w, bias, resid, gamma, beta, 1e-5, y, zero, row_mask=mask)
+    plain = resid0.clone()
+    _capi.linear(a, w, bias, _capi.EPI_RESIDUAL_ZERO if zero else _capi.EPI_RESIDUAL, plain, row_mask=mask,
+                 tile_n=tile)
+    assert torch.equal(resid, plain)
+    y_sep = torch.empty_like(y)
+    _capi.layernorm(plain, gamma, beta, 1e-5, y_sep)
+    diff = (y.float() - y_sep.float()).abs()
+    assert bool((diff <= y_sep.float().abs() * 2.0**-7 + 1e-6).all()), float(diff.max())
+    assert (diff > 0).float().mean().item() < 0.01
+    ref = F.layer_norm(plain, (n,), gamma.float(), beta.float(), 1e-5)
+    torch.testing.assert_close(y.float(), ref, atol=1e-2, rtol=8e-3)
+
+
+def test_gemm_residual_layernorm_is_row_invariant_and_deterministic():
+    """A row's output does not depend on how many rows share the launch, and repeats bit for bit."""
+    m, n, k = 2048, 1024, 1024
+    a, w, bias, _ = _gemm_inputs(m, n, k, 9)
+    g = _gen(10)
+    resid0 = torch.randn(m, n, device="cuda", generator=g)
+    gamma = (torch.randn(n, device="cuda", generator=g) * 0.2 + 1).bfloat16()
+    beta = (torch.randn(n, device="cuda", generator=g) * 0.1).bfloat16()
+    outs = []
+    for rows in (m, m, 384):
+        r = resid0[:rows].clone()
+        y = torch.empty(rows, n, device="cuda", dtype=torch.bfloat16)
+        _capi.linear_ln(a[:rows].contiguous(), w, bias, r, gamma, beta, 1e-5, y, True)
+        outs.append((r, y))
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+    assert torch.equal(outs[0][0][:384], outs[2][0]) and torch.equal(outs[0][1][:384], outs[2][1])

@@ -181,3 +181,30 @@ def test_weight_update_recaptures_graph():
         b_e = model(x)
     assert not torch.equal(a, b)
     assert torch.equal(b, b_e)
+
+
+@pytest.mark.parametrize("key,batch,seq_len", [("c1", None, None), ("c2", None, None), ("c3", 2, 1024),
+                                               ("c5", 1, 4096)])
+def test_layernorm_fused_and_separate_agree(key, batch, seq_len):
+    """norm2 / norm1 inside the residual GEMMs (b2_linear_ln_fwd) against separate LayerNorm
+    launches: both pass the gate against the oracle and stay within it of each other."""
+    cfg, pad = _baseline_case(key, batch, seq_len)
+    state = oracle.round_state_to_bf16(oracle.build_reference_state(cfg, 0))
+    x, mask = oracle.generate_random_case(cfg, torch.device("cuda"), torch.float32, 0, pad)
+    xb = x.bfloat16()
+    model = _model(cfg, state)
+    outs = {}
+    with torch.inference_mode():
+        for mode in (True, False):
+            model.fuse_layernorm = mode
+            outs[mode] = model(xb, mask)
+    assert model.layernorm_fused(xb.shape[0] * xb.shape[1]) is False
+    model.fuse_layernorm = True
+    assert model.layernorm_fused(xb.shape[0] * xb.shape[1]) is True
+    ref = _oracle_gpu(state, cfg, xb, mask)
+    for mode, y in outs.items():
+        gate = baseline_gate(y, ref)
+        assert gate.passed, (mode, gate)
+    assert baseline_gate(outs[True], outs[False].float()).passed
+    if pad > 0:
+        assert torch.all(outs[True][~mask] == 0)

@@ -47,6 +47,15 @@ SIGNATURES = {
         ctypes.c_int,
         [_vp, _vp, _vp, _i64, _i64, _i64, ctypes.c_int, _vp, _i64, _vp, ctypes.c_int, _vp],
     ),
+    "b2_linear_ln_fwd": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _i64, _i64, _i64, ctypes.c_int, _vp, _vp, _vp, _vp, ctypes.c_float, _vp, _vp],
+    ),
+    "b2_linear_ln_plan": (
+        ctypes.c_int,
+        [_i64, _i64, _i64, ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
+         ctypes.POINTER(ctypes.c_int)],
+    ),
     "b2_attention_fwd": (
         ctypes.c_int,
         [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, ctypes.c_int, ctypes.c_float, _vp, _i64, _vp],
@@ -229,6 +238,56 @@ def linear(
         _stream_ptr(a.device),
     )
     _check(status, "b2_linear_fwd")
+
+
+def linear_ln_plan(m: int, n: int, k: int, sm_count: int = 0) -> Optional[Tuple[int, int, bool]]:
+    """(tile_n, cluster, recommended) of b2_linear_ln_fwd for an m x n x k problem, or None when n
+    has no fused plan (see b2_linear_ln_plan). sm_count 0 asks the current device."""
+    lib = load_library()
+    tile, cluster, rec = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
+    status = lib.b2_linear_ln_plan(int(m), int(n), int(k), int(sm_count), ctypes.byref(tile), ctypes.byref(cluster),
+                                   ctypes.byref(rec))
+    if status == 2:
+        return None
+    _check(status, "b2_linear_ln_plan")
+    return int(tile.value), int(cluster.value), bool(rec.value)
+
+
+def linear_ln(
+    a: torch.Tensor,
+    w: torch.Tensor,
+    bias: Optional[torch.Tensor],
+    resid: torch.Tensor,
+    gamma: torch.Tensor,
+    beta: torch.Tensor,
+    eps: float,
+    ln_out: torch.Tensor,
+    zero_masked_rows: bool,
+    row_mask: Optional[torch.Tensor] = None,
+) -> None:
+    """resid = mask ? resid + a @ w.T + bias : (0 | resid); ln_out = LayerNorm(resid) (b2_linear_ln_fwd)."""
+    _require(a, torch.bfloat16, "a")
+    _require(w, torch.bfloat16, "w")
+    _require(resid, torch.float32, "resid")
+    _require(gamma, torch.bfloat16, "gamma")
+    _require(beta, torch.bfloat16, "beta")
+    _require(ln_out, torch.bfloat16, "ln_out")
+    k = a.shape[-1]
+    m = a.numel() // k
+    n = w.shape[0]
+    if w.shape[1] != k:
+        raise ValueError(f"w has shape {tuple(w.shape)}, expected [n, {k}]")
+    if resid.numel() != m * n or ln_out.numel() != m * n or resid.shape[-1] != n:
+        raise ValueError(f"resid and ln_out must be [{m}, {n}]")
+    if bias is not None:
+        _require(bias, torch.bfloat16, "bias")
+    if row_mask is not None:
+        _require(row_mask, torch.uint8, "row_mask")
+    status = load_library().b2_linear_ln_fwd(
+        _ptr(a), _ptr(w), _ptr(bias), m, n, k, 1 if zero_masked_rows else 0, _ptr(resid), _ptr(row_mask), _ptr(gamma),
+        _ptr(beta), float(eps), _ptr(ln_out), _stream_ptr(a.device),
+    )
+    _check(status, "b2_linear_ln_fwd")
 
 
 def attention(

@@ -162,6 +162,47 @@ B2_API int b2_linear_fwd(const void* a, const void* w, const void* bias, int64_t
                       "b2_linear_fwd");
 }
 
+B2_API int b2_linear_ln_plan(int64_t m, int64_t n, int64_t k, int sm_count, int* tile_n, int* cluster,
+                             int* recommended) {
+  if (m <= 0 || n <= 0 || k <= 0) return fail(1, "b2_linear_ln_plan: invalid shape");
+  int sms = sm_count;
+  if (sms <= 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return fail(2, "b2_linear_ln_plan: no CUDA device and no sm_count");
+    sms = device_sm_count(dev);
+  }
+  if (m > 0x7fffff00LL || n > 0x7fffff00LL) return fail(2, "b2_linear_ln_plan: dimension exceeds 2^31");
+  if (!gemm_ln_plan(m, n, k, sms, tile_n, cluster, recommended))
+    return fail(2, "b2_linear_ln_plan: n=%lld has no fused plan (n %% 32 == 0 and n <= 256 or n = {128,192,256} x c, "
+                "c <= 8)", (long long)n);
+  return 0;
+}
+
+B2_API int b2_linear_ln_fwd(const void* a, const void* w, const void* bias, int64_t m, int64_t n, int64_t k,
+                            int zero_masked_rows, float* resid, const uint8_t* row_mask, const void* gamma,
+                            const void* beta, float eps, void* ln_out, void* stream) {
+  if (a == nullptr || w == nullptr || resid == nullptr || gamma == nullptr || beta == nullptr || ln_out == nullptr)
+    return fail(1, "b2_linear_ln_fwd: null pointer argument");
+  if (m < 0 || n <= 0 || k <= 0) return fail(1, "b2_linear_ln_fwd: invalid shape m=%lld n=%lld k=%lld", (long long)m,
+                                             (long long)n, (long long)k);
+  if (!(eps > 0.f)) return fail(1, "b2_linear_ln_fwd: eps must be positive");
+  if (k % 8 != 0) return fail(2, "b2_linear_ln_fwd: k=%lld must be a multiple of 8", (long long)k);
+  if (m > 0x7fffff00LL || n > 0x7fffff00LL) return fail(2, "b2_linear_ln_fwd: dimension exceeds 2^31");
+  if (!gemm_ln_plan(m > 0 ? m : 1, n, k, 0, nullptr, nullptr, nullptr))
+    return fail(2, "b2_linear_ln_fwd: n=%lld has no fused plan (see b2_linear_ln_plan)", (long long)n);
+  if (!aligned16(a) || !aligned16(w) || !aligned16(resid) || !aligned16(ln_out) || !aligned16(gamma) ||
+      !aligned16(beta) || (bias && !aligned16(bias)))
+    return fail(2, "b2_linear_ln_fwd: pointers must be 16-byte aligned");
+  if (m == 0) return 0;
+  if (!is_sm100(nullptr)) return fail(2, "b2_linear_ln_fwd: needs an sm_100 (B200) device");
+  return check_launch(launch_gemm_ln(static_cast<const __nv_bfloat16*>(a), static_cast<const __nv_bfloat16*>(w),
+                                     static_cast<const __nv_bfloat16*>(bias), m, n, k, zero_masked_rows != 0, resid,
+                                     row_mask, static_cast<const __nv_bfloat16*>(gamma),
+                                     static_cast<const __nv_bfloat16*>(beta), eps, static_cast<__nv_bfloat16*>(ln_out),
+                                     static_cast<cudaStream_t>(stream)),
+                      "b2_linear_ln_fwd");
+}
+
 B2_API int b2_attention_rows_fwd(const void* qkv, int64_t ld_qkv, int64_t q_col, int64_t k_col, int64_t v_col,
                                  int64_t batch, int64_t seq_len, int64_t num_heads, int64_t head_dim,
                                  const int32_t* kv_len, int causal, float scale, const int64_t* q_ranges,

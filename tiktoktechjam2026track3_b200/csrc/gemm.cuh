@@ -15,6 +15,14 @@
 // rank that owns the row (row / rows_per_rank) with system-scope atomics, over NVLink for the
 // other ranks' rows, while the rest of the GEMM still runs; the caller passes the bias on one
 // rank only and orders the owners' reads with cross-GPU barriers before and after the GEMM.
+//   kEpiResidualLn      kEpiResidual, then ln_out_bf16 = LayerNorm(res_f32 row)        (out_proj + norm2)
+//   kEpiResidualZeroLn  kEpiResidualZero, then ln_out_bf16 = LayerNorm(res_f32 row)    (ffn_out + next norm1)
+// The two *Ln epilogues need whole rows: they run as clusters of N / BN CTAs, CTA r of a cluster
+// computing column block r of the same 128 rows, and exchange per-row partial sums through
+// distributed shared memory (two rounds: the sum, then the sum of squared deviations from the
+// mean, as nn.LayerNorm's biased variance; every CTA adds the partials in the same fixed order,
+// so all of them normalise a row with bit-identical statistics). The residual tile is written
+// back into the TMEM accumulator between the rounds, so it is read from HBM once.
 // A is [M, K] row-major bf16 (tokens x features), W is [N, K] row-major bf16 (nn.Linear layout,
 // i.e. K-major for the B operand), the residual stream is fp32 [M, ldo].
 //
@@ -27,6 +35,7 @@
 //               op, stores to global memory.
 // Two TMEM accumulators (2 x BN fp32 columns) let the epilogue of tile i overlap the main loop
 // of tile i+1.
+#include <atomic>
 #include <cstring>
 #include <mutex>
 
@@ -44,6 +53,8 @@ enum GemmEpilogue : int {
   kEpiRsResidual = 5,
   kEpiRsResidualZero = 6,
   kEpiBiasPeers = 7,
+  kEpiResidualLn = 8,
+  kEpiResidualZeroLn = 9,
 };
 
 constexpr int kGemmMaxPeers = 8;
@@ -59,6 +70,11 @@ struct GemmParams {
   // kEpiBiasPeers: every rank's output base; columns >= peer_col go to every rank's copy.
   void* peer_out[kGemmMaxPeers];
   int rows_per_rank, world, rank, peer_col;
+  // kEpi*Ln: LayerNorm of the updated residual rows into ln_out [M, N] bf16 (row stride N).
+  const __nv_bfloat16* ln_gamma;
+  const __nv_bfloat16* ln_beta;
+  __nv_bfloat16* ln_out;
+  float ln_eps;
 };
 
 constexpr int kGemmBM = 128;
@@ -82,6 +98,16 @@ template <int EPI>
 __host__ __device__ constexpr bool is_rs_epi() {
   return EPI == kEpiRsResidual || EPI == kEpiRsResidualZero;
 }
+template <int EPI>
+__host__ __device__ constexpr bool is_ln_epi() {
+  return EPI == kEpiResidualLn || EPI == kEpiResidualZeroLn;
+}
+
+// Row-statistics exchange of the *Ln epilogues: 8 mbarriers (2 rounds x 4 TMEM lane quadrants)
+// and the partial sums [round][quadrant][source = 2 * cluster rank + column half][32 rows].
+constexpr int kLnMaxCluster = 8;
+constexpr int kLnBarrierBytes = 128;
+constexpr int kLnBytes = kLnBarrierBytes + 2 * 4 * (2 * kLnMaxCluster) * 32 * 4;
 
 // Epilogue staging: TMEM gives each lane one row of the accumulator, so a lane writing its own
 // row would make every warp-wide global access touch 32 different rows (32 memory transactions
@@ -92,10 +118,13 @@ constexpr int kEpiStageBytes = (kGemmThreads / 32 - 2) * 32 * 32 * 4;
 
 template <int BN, int EPI>
 struct GemmSmem {
-  static constexpr int kStages = BN == 192 ? 4 : GemmCfg<BN>::kStages;
-  static constexpr int kBytes =
-      kStages * GemmCfg<BN>::kStageBytes + 1024 + GemmCfg<BN>::kBarrierBytes + kEpiStageBytes;
-  static_assert(kBytes <= 232448, "shared memory per CTA");
+  static constexpr int kFixed =
+      1024 + GemmCfg<BN>::kBarrierBytes + kEpiStageBytes + (is_ln_epi<EPI>() ? kLnBytes : 0);
+  static constexpr int kWant = BN == 192 ? 4 : GemmCfg<BN>::kStages;
+  static constexpr int kFit = (232448 - kFixed) / GemmCfg<BN>::kStageBytes;
+  static constexpr int kStages = kWant < kFit ? kWant : kFit;
+  static constexpr int kBytes = kStages * GemmCfg<BN>::kStageBytes + kFixed;
+  static_assert(kStages >= 3 && kBytes <= 232448, "shared memory per CTA");
 };
 
 __device__ __forceinline__ float4 load_bias4(const __nv_bfloat16* bias, int col) {
@@ -190,6 +219,102 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmParams& p, int row
   __syncwarp();
 }
 
+// Pass 1 of the *Ln epilogues for one warp's 32 rows x 32 columns (layout as in
+// gemm_epilogue_chunk): updates and stores the fp32 residual, returns the updated values in
+// `vals` (lane i: rows 4j + i / 8, columns 4(i % 8) .. +3, j = 0..7, as vals[4j .. 4j+3]) and adds
+// each row's 4 values to part[j]. Masked rows keep their residual (kEpiResidualLn) or become 0
+// (kEpiResidualZeroLn); either way they are normalised like the others, as nn.LayerNorm does.
+template <int EPI>
+__device__ __forceinline__ void gemm_ln_chunk(const GemmParams& p, int row0, int col0, float (&vals)[32],
+                                              float4* stage, float (&part)[8]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    stage[lane * 8 + (c ^ (lane & 7))] = make_float4(vals[4 * c], vals[4 * c + 1], vals[4 * c + 2], vals[4 * c + 3]);
+  __syncwarp();
+  const int q = lane & 7;
+  const int col = col0 + 4 * q;
+  const float4 b = load_bias4(p.bias, col);
+  float4 v[8], res[8];
+  bool live[8], keep[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = i * 4 + (lane >> 3);
+    const int row = row0 + r;
+    v[i] = stage[r * 8 + (q ^ (r & 7))];
+    live[i] = row < p.M;
+    keep[i] = live[i] && (p.row_mask == nullptr || p.row_mask[row] != 0);
+    res[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t off = static_cast<int64_t>(row0 + i * 4 + (lane >> 3)) * p.ldo + col;
+    const bool need = EPI == kEpiResidualLn ? live[i] : keep[i];
+    if (need) res[i] = *reinterpret_cast<const float4*>(static_cast<const float*>(p.out) + off);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t off = static_cast<int64_t>(row0 + i * 4 + (lane >> 3)) * p.ldo + col;
+    float4 o = res[i];
+    if (keep[i]) {
+      o.x += v[i].x + b.x;
+      o.y += v[i].y + b.y;
+      o.z += v[i].z + b.z;
+      o.w += v[i].w + b.w;
+    }
+    if (keep[i] || (EPI == kEpiResidualZeroLn && live[i])) *reinterpret_cast<float4*>(static_cast<float*>(p.out) + off) = o;
+    vals[4 * i] = o.x;
+    vals[4 * i + 1] = o.y;
+    vals[4 * i + 2] = o.z;
+    vals[4 * i + 3] = o.w;
+    part[i] += (o.x + o.y) + (o.z + o.w);
+  }
+  __syncwarp();
+}
+
+// Completes one round of the *Ln row statistics: part[j] holds this lane's partial sum for row
+// 4j + lane / 8 of the warp's 32 rows (over its columns of this CTA's tile). Sums it over the 8
+// lanes of the row, over the two column halves of the quadrant and over the cluster's CTAs, and
+// returns the row totals in tot[j] (identical bits in every CTA: fixed summation order). Returns
+// false when the wait for the other CTAs gave up (status recorded, *abort raised).
+__device__ __forceinline__ bool gemm_ln_allreduce(float (&part)[8], float (&tot)[8], int round, int quad, int half,
+                                                  uint32_t parity, int cs, uint32_t my_rank, uint64_t* xbar,
+                                                  float* xch, volatile int* abort) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    part[j] += __shfl_xor_sync(0xffffffffu, part[j], 1);
+    part[j] += __shfl_xor_sync(0xffffffffu, part[j], 2);
+    part[j] += __shfl_xor_sync(0xffffffffu, part[j], 4);
+  }
+  // Lane L takes row L: row 4j + g is held by the lanes 8g .. 8g+7, j = L / 4, g = L % 4.
+  float mine = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float t = __shfl_sync(0xffffffffu, part[j], (lane & 3) << 3);
+    if ((lane >> 2) == j) mine = t;
+  }
+  float* block = xch + (round * 4 + quad) * (2 * kLnMaxCluster) * 32;
+  uint64_t* bar = &xbar[round * 4 + quad];
+  const uint32_t slot = smem_u32(block + (2 * static_cast<int>(my_rank) + half) * 32 + lane);
+  for (int r = 0; r < cs; ++r) {
+    uint32_t dst, dbar;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(dst) : "r"(slot), "r"(r));
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(dbar) : "r"(smem_u32(bar)), "r"(r));
+    st_cluster_f32(dst, mine);
+    mbar_arrive_cluster(dbar);  // release: orders the store above before the arrival
+  }
+  if (!mbar_wait_cluster(bar, parity, abort, kKernelGemm, 6 + round)) return false;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float* rowp = block + j * 4 + (lane >> 3);
+    float t = 0.f;
+    for (int src = 0; src < 2 * cs; ++src) t += rowp[src * 32];
+    tot[j] = t;
+  }
+  return true;
+}
+
 // Waits for a phase without looking at the abort flag (used only on the abort path, to let
 // copies and MMAs that are still in flight land before the CTA releases its memory).
 __device__ __forceinline__ void mbar_drain_wait(uint64_t* bar, uint32_t parity) {
@@ -231,6 +356,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
+    if constexpr (is_ln_epi<EPI>()) {
+      uint64_t* xbar = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(full) + Cfg::kBarrierBytes +
+                                                   kEpiStageBytes);
+      // Every quadrant warp (2 per CTA) of every CTA of the cluster arrives once per lane.
+      for (int i = 0; i < 8; ++i) mbar_init(&xbar[i], 2 * p.n_blocks * 32);
+    }
     fence_mbarrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -242,7 +373,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tmem_relinquish();
   }
   tc_fence_before_sync();
-  __syncthreads();
+  if constexpr (is_ln_epi<EPI>())
+    cluster_sync_all();  // every CTA's exchange barriers exist before any remote arrive
+  else
+    __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
   pdl_wait_previous_grid();
@@ -348,13 +482,80 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int row = m_blk * kGemmBM + row_in_tile;
       const uint32_t t_row =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * Cfg::kAccStride);
+      if constexpr (is_ln_epi<EPI>()) {
+        // Round 1: residual update, stored to HBM and written back over the accumulator; row sums.
+        uint64_t* xbar = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(full) + Cfg::kBarrierBytes +
+                                                     kEpiStageBytes);
+        float* xch = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xbar) + kLnBarrierBytes);
+        const uint32_t my_rank = static_cast<uint32_t>(n_blk);  // == %cluster_ctarank
+        const uint32_t parity = static_cast<uint32_t>(local & 1);
+        const float inv_d = 1.0f / static_cast<float>(p.N);
+        float part[8], mean[8], rstd[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) part[j] = 0.f;
 #pragma unroll 1
-      for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
-        const int col0 = n_blk * BN + c * 32;
-        if (col0 >= p.N) break;  // warp-uniform
-        float v[32];
-        tmem_load_32cols(t_row + c * 32, v);
-        gemm_epilogue_chunk<EPI>(p, row - lane, col0, v, epi_stage);
+        for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+          const int col0 = n_blk * BN + c * 32;
+          if (col0 >= p.N) break;  // warp-uniform
+          float v[32];
+          tmem_load_32cols(t_row + c * 32, v);
+          gemm_ln_chunk<EPI>(p, row - lane, col0, v, epi_stage, part);
+          tmem_store_32cols(t_row + c * 32, v);
+        }
+        if (!gemm_ln_allreduce(part, mean, 0, quad, half, parity, p.n_blocks, my_rank, xbar, xch, abort_flag)) break;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          mean[j] *= inv_d;
+          part[j] = 0.f;
+        }
+        // Round 2: sum of squared deviations.
+#pragma unroll 1
+        for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+          if (n_blk * BN + c * 32 >= p.N) break;
+          float v[32];
+          tmem_load_32cols(t_row + c * 32, v);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float d = v[4 * j + e] - mean[j];
+              part[j] = fmaf(d, d, part[j]);
+            }
+        }
+        if (!gemm_ln_allreduce(part, rstd, 1, quad, half, parity, p.n_blocks, my_rank, xbar, xch, abort_flag)) break;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) rstd[j] = rsqrtf(rstd[j] * inv_d + p.ln_eps);
+        // Normalise: y = (x - mean) * rstd * gamma + beta, bf16, row segments of 8 lanes x 4 columns.
+#pragma unroll 1
+        for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+          const int col0 = n_blk * BN + c * 32;
+          if (col0 >= p.N) break;
+          float v[32];
+          tmem_load_32cols(t_row + c * 32, v);
+          const int col = col0 + 4 * (lane & 7);
+          const float4 g = load_bias4(p.ln_gamma, col);
+          const float4 bt = load_bias4(p.ln_beta, col);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int r = row - lane + j * 4 + (lane >> 3);
+            if (r >= p.M) continue;
+            const float y0 = fmaf((v[4 * j] - mean[j]) * rstd[j], g.x, bt.x);
+            const float y1 = fmaf((v[4 * j + 1] - mean[j]) * rstd[j], g.y, bt.y);
+            const float y2 = fmaf((v[4 * j + 2] - mean[j]) * rstd[j], g.z, bt.z);
+            const float y3 = fmaf((v[4 * j + 3] - mean[j]) * rstd[j], g.w, bt.w);
+            *reinterpret_cast<uint2*>(p.ln_out + static_cast<int64_t>(r) * p.N + col) =
+                make_uint2(pack_bf16x2(y0, y1), pack_bf16x2(y2, y3));
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+          const int col0 = n_blk * BN + c * 32;
+          if (col0 >= p.N) break;  // warp-uniform
+          float v[32];
+          tmem_load_32cols(t_row + c * 32, v);
+          gemm_epilogue_chunk<EPI>(p, row - lane, col0, v, epi_stage);
+        }
       }
       tc_fence_before_sync();
       mbar_arrive(&acc_empty[acc]);
@@ -363,6 +564,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 
   __syncthreads();
+  if constexpr (is_ln_epi<EPI>()) cluster_sync_all();  // no CTA leaves while others may still write to it
   if (warp == 1) {
     tc_fence_after_sync();
     tmem_dealloc(tmem_base, Cfg::kTmemCols);
@@ -738,6 +940,129 @@ cudaError_t launch_gemm(const __nv_bfloat16* A, const __nv_bfloat16* W, const __
   if (bn == 256) return dispatch_epi<256>(epi, ta, tb, p, grid, stream);
   if (bn == 192) return dispatch_epi<192>(epi, ta, tb, p, grid, stream);
   return dispatch_epi<128>(epi, ta, tb, p, grid, stream);
+}
+
+// ---------------------------------------------------------------------------------------------
+// GEMM + residual + LayerNorm (kEpiResidualLn / kEpiResidualZeroLn): clusters of N / BN CTAs.
+// ---------------------------------------------------------------------------------------------
+// Picks the column tile of the LayerNorm-fused GEMM. The cluster spans the row (cs = N / bn <= 8
+// CTAs) and each row's statistics are summed in an order fixed by bn, so the choice depends on N
+// alone — never on M — to keep every row's output independent of how many rows share the launch
+// (batch shards give the same bits as the full batch): n <= 256 takes one CTA; otherwise a
+// power-of-two cluster is preferred, then the widest tile. *recommended is 1 where the fused
+// launch is expected to beat GEMM + separate LayerNorm: everywhere but the 256-wide tiles of wide
+// rows, whose shared memory (LayerNorm exchange + epilogue staging) leaves a 3-deep operand ring.
+bool gemm_ln_plan(int64_t M, int64_t N, int64_t K, int sms, int* bn_out, int* cs_out, int* recommended) {
+  (void)sms;
+  if (M <= 0 || N <= 0 || K <= 0 || N % 32 != 0) return false;
+  int bn = 0, cs = 0;
+  if (N <= 256) {
+    bn = N <= 128 ? 128 : (N <= 192 ? 192 : 256);
+    cs = 1;
+  } else {
+    const int cand[3] = {256, 192, 128};
+    for (int pow2 = 1; pow2 >= 0 && cs == 0; --pow2) {
+      for (int i = 0; i < 3 && cs == 0; ++i) {
+        if (N % cand[i] != 0) continue;
+        const int c = static_cast<int>(N / cand[i]);
+        if (c > kLnMaxCluster || (pow2 && (c & (c - 1)) != 0)) continue;
+        bn = cand[i];
+        cs = c;
+      }
+    }
+    if (cs == 0) return false;
+  }
+  if (bn_out) *bn_out = bn;
+  if (cs_out) *cs_out = cs;
+  if (recommended) *recommended = (bn != 256 || cs == 1) ? 1 : 0;
+  return true;
+}
+
+template <int BN, int EPI>
+static cudaError_t launch_gemm_ln_t(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int cs,
+                                    cudaStream_t stream) {
+  static std::once_flag once[64];
+  static std::atomic<int> max_clusters[64][kLnMaxCluster + 1];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaError_t attr_err = cudaSuccess;
+  std::call_once(once[dev & 63], [&] {
+    attr_err = cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    GemmSmem<BN, EPI>::kBytes);
+  });
+  if (attr_err != cudaSuccess) return attr_err;
+  cudaLaunchConfig_t config = {};
+  config.blockDim = dim3(kGemmThreads);
+  config.dynamicSmemBytes = GemmSmem<BN, EPI>::kBytes;
+  config.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(cs);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  config.attrs = attr;
+  config.numAttrs = 2;
+  // The kernel is persistent: at most as many clusters as can be resident at once.
+  std::atomic<int>& cached = max_clusters[dev & 63][cs];
+  int resident = cached.load();
+  if (resident == 0) {
+    config.gridDim = dim3(static_cast<unsigned>(cs * p.m_blocks));
+    const cudaError_t e = cudaOccupancyMaxActiveClusters(&resident, gemm_tc_kernel<BN, EPI>, &config);
+    if (e != cudaSuccess) return e;
+    if (resident <= 0) return cudaErrorInvalidConfiguration;
+    cached.store(resident);
+  }
+  const int clusters = p.m_blocks < resident ? p.m_blocks : resident;
+  config.gridDim = dim3(static_cast<unsigned>(cs * clusters));
+  return cudaLaunchKernelEx(&config, gemm_tc_kernel<BN, EPI>, ta, tb, p);
+}
+
+template <int BN>
+static cudaError_t dispatch_ln(bool zero_masked, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
+                               int cs, cudaStream_t stream) {
+  return zero_masked ? launch_gemm_ln_t<BN, kEpiResidualZeroLn>(ta, tb, p, cs, stream)
+                     : launch_gemm_ln_t<BN, kEpiResidualLn>(ta, tb, p, cs, stream);
+}
+
+// resid[M, N] (fp32) += A W^T + bias on kept rows (kept rows only, or kept rows and zeros when
+// zero_masked), then ln_out[M, N] = LayerNorm(resid) with gamma / beta / eps, in one launch.
+cudaError_t launch_gemm_ln(const __nv_bfloat16* A, const __nv_bfloat16* W, const __nv_bfloat16* bias, int64_t M,
+                           int64_t N, int64_t K, bool zero_masked, float* resid, const uint8_t* row_mask,
+                           const __nv_bfloat16* gamma, const __nv_bfloat16* beta, float eps, __nv_bfloat16* ln_out,
+                           cudaStream_t stream) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int sms = device_sm_count(dev);
+  int bn = 0, cs = 0;
+  if (!gemm_ln_plan(M, N, K, sms, &bn, &cs, nullptr)) return cudaErrorInvalidValue;
+  CUtensorMap ta, tb;
+  cudaError_t e = make_tmap_bf16_2d(&ta, A, K, M, K * 2, kGemmBK, kGemmBM);
+  if (e != cudaSuccess) return e;
+  e = make_tmap_bf16_2d(&tb, W, K, N, K * 2, kGemmBK, bn);
+  if (e != cudaSuccess) return e;
+  GemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.out = resid;
+  p.ldo = N;
+  p.bias = bias;
+  p.row_mask = row_mask;
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.m_blocks = static_cast<int>((M + kGemmBM - 1) / kGemmBM);
+  p.n_blocks = static_cast<int>((N + bn - 1) / bn);
+  p.k_blocks = static_cast<int>((K + kGemmBK - 1) / kGemmBK);
+  p.world = 1;
+  p.ln_gamma = gamma;
+  p.ln_beta = beta;
+  p.ln_out = ln_out;
+  p.ln_eps = eps;
+  if (p.n_blocks != cs) return cudaErrorInvalidValue;
+  if (bn == 256) return dispatch_ln<256>(zero_masked, ta, tb, p, cs, stream);
+  if (bn == 192) return dispatch_ln<192>(zero_masked, ta, tb, p, cs, stream);
+  return dispatch_ln<128>(zero_masked, ta, tb, p, cs, stream);
 }
 
 }  // namespace b2

@@ -170,6 +170,12 @@ class UserOptimizedTransformer(nn.Module):
         # exactly the kernels the eager path launches). Keyed by shape, device and mask presence.
         self.use_cuda_graph = True
         self._graphs: Dict[tuple, "_GraphedStack"] = {}
+        # LayerNorm fused into the residual GEMMs (b2_linear_ln_fwd): "auto" where the library
+        # recommends it for d_model, True / False to force it on (where d_model has a plan) or off.
+        # The choice depends on the model's widths only, never on the token count, so a batch shard
+        # computes its rows exactly as the full batch does.
+        self.fuse_layernorm = "auto"
+        self._fused_cache: Dict[tuple, bool] = {}
 
     # ------------------------------------------------------------------ weights
     def _weights_key(self) -> tuple:
@@ -230,6 +236,25 @@ class UserOptimizedTransformer(nn.Module):
         end.record()
         self._launch_log.append((kind, start, end))
 
+    def layernorm_fused(self, tokens: int) -> bool:
+        """Whether a forward over `tokens` rows runs norm2 and the next block's norm1 inside the
+        out_proj / ffn_out GEMMs (b2_linear_ln_fwd) instead of as LayerNorm launches. Depends on
+        d_model and the mode only (tokens > 0 just needs a valid plan query)."""
+        mode = self.fuse_layernorm
+        if mode is False or tokens <= 0:
+            return False
+        hit = self._fused_cache.get(mode)
+        if hit is None:
+            cfg = self.config
+            plans = [_capi.linear_ln_plan(1, cfg.d_model, cfg.d_model, sm_count=1),
+                     _capi.linear_ln_plan(1, cfg.d_model, cfg.ffn_dim, sm_count=1)]
+            if any(p is None for p in plans):
+                hit = False
+            else:
+                hit = True if mode is True else all(p[2] for p in plans)
+            self._fused_cache[mode] = hit
+        return hit
+
     # ------------------------------------------------------------------ forward
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
         cfg: TransformerConfig = self.config
@@ -264,12 +289,13 @@ class UserOptimizedTransformer(nn.Module):
         cfg = self.config
         tokens, d = batch * seq_len, cfg.d_model
         out = torch.empty(batch, seq_len, d, device=x.device, dtype=torch.bfloat16)
+        fused = self.layernorm_fused(tokens)
         if self.use_cuda_graph and self._launch_log is None:
-            shape_key = (batch, seq_len, x.device, kv_len is not None)
+            shape_key = (batch, seq_len, x.device, kv_len is not None, fused)
             stack = self._graphs.get(shape_key)
             if stack is None or stack.packed is not packed:  # new shape, or weights changed: (re)capture
                 self._graphs.pop(shape_key, None)
-                stack = _GraphedStack(self, batch, seq_len, x.device, kv_len is not None, packed)
+                stack = _GraphedStack(self, batch, seq_len, x.device, kv_len is not None, packed, fused)
                 self._graphs[shape_key] = stack
             stack.run(x.view(tokens, d), kv_len, row_mask, out.view(tokens, d))
             return out
@@ -277,36 +303,49 @@ class UserOptimizedTransformer(nn.Module):
         pb0 = packed[0]
         self._timed("layernorm", _capi.layernorm, x.view(tokens, d), pb0.ln1_w, pb0.ln1_b, pb0.ln1_eps, ws.ln,
                     resid_out=ws.resid)
-        self._blocks(ws, batch, seq_len, kv_len, row_mask, packed)
+        self._blocks(ws, batch, seq_len, kv_len, row_mask, packed, fused)
         fn = self.final_norm
         self._timed("layernorm", _capi.layernorm, ws.resid, fn.weight, fn.bias, float(fn.eps), out.view(tokens, d),
                     row_mask=row_mask)
         return out
 
-    def _blocks(self, ws: "_Workspace", batch: int, seq_len: int, kv_len, row_mask, packed) -> None:
-        """Every launch between the first LayerNorm (done) and the final LayerNorm."""
+    def _blocks(self, ws: "_Workspace", batch: int, seq_len: int, kv_len, row_mask, packed, fused: bool) -> None:
+        """Every launch between the first LayerNorm (done) and the final LayerNorm.
+
+        With `fused`, norm2 runs in out_proj's epilogue and the next block's norm1 in ffn_out's
+        (b2_linear_ln_fwd); the last block's ffn_out is the plain residual GEMM.
+        """
         cfg = self.config
         d, h, hd = cfg.d_model, cfg.num_heads, cfg.head_dim
         scale = hd**-0.5
         t = self._timed
         for i, pb in enumerate(packed):
-            if i > 0:
+            if i > 0 and not fused:
                 t("layernorm", _capi.layernorm, ws.resid, pb.ln1_w, pb.ln1_b, pb.ln1_eps, ws.ln)
             t("gemm_qkv", _capi.linear, ws.ln, pb.w_qkv, pb.b_qkv, _capi.EPI_BIAS, ws.qkv)
             t("attention", _capi.attention, ws.qkv, batch, seq_len, h, hd, 0, d, 2 * d, kv_len, cfg.causal, scale,
               ws.ctx)
-            t("gemm_out", _capi.linear, ws.ctx, pb.w_o, pb.b_o, _capi.EPI_RESIDUAL, ws.resid, row_mask)
-            t("layernorm", _capi.layernorm, ws.resid, pb.ln2_w, pb.ln2_b, pb.ln2_eps, ws.ln)
+            if fused:
+                t("gemm_out", _capi.linear_ln, ws.ctx, pb.w_o, pb.b_o, ws.resid, pb.ln2_w, pb.ln2_b, pb.ln2_eps, ws.ln,
+                  False, row_mask)
+            else:
+                t("gemm_out", _capi.linear, ws.ctx, pb.w_o, pb.b_o, _capi.EPI_RESIDUAL, ws.resid, row_mask)
+                t("layernorm", _capi.layernorm, ws.resid, pb.ln2_w, pb.ln2_b, pb.ln2_eps, ws.ln)
             t("gemm_ffn_in", _capi.linear, ws.ln, pb.w_1, pb.b_1, _capi.EPI_BIAS_GELU, ws.hidden)
-            t("gemm_ffn_out", _capi.linear, ws.hidden, pb.w_2, pb.b_2, _capi.EPI_RESIDUAL_ZERO, ws.resid, row_mask)
+            if fused and i + 1 < len(packed):
+                nxt = packed[i + 1]
+                t("gemm_ffn_out", _capi.linear_ln, ws.hidden, pb.w_2, pb.b_2, ws.resid, nxt.ln1_w, nxt.ln1_b,
+                  nxt.ln1_eps, ws.ln, True, row_mask)
+            else:
+                t("gemm_ffn_out", _capi.linear, ws.hidden, pb.w_2, pb.b_2, _capi.EPI_RESIDUAL_ZERO, ws.resid, row_mask)
 
     def release_graphs(self) -> None:
         """Drops captured CUDA graphs and their static buffers."""
         self._graphs.clear()
 
     @staticmethod
-    def launches_per_forward(num_layers: int) -> int:
-        return 7 * num_layers + 1
+    def launches_per_forward(num_layers: int, fused: bool = False) -> int:
+        return 5 * num_layers + 2 if fused else 7 * num_layers + 1
 
 
 class _Workspace:
@@ -330,7 +369,7 @@ class _GraphedStack:
     """
 
     def __init__(self, model: "UserOptimizedTransformer", batch: int, seq_len: int, device: torch.device,
-                 masked: bool, packed: List[_PackedBlock]) -> None:
+                 masked: bool, packed: List[_PackedBlock], fused: bool) -> None:
         self.model = model
         self.packed = packed
         self.ws = _Workspace(model.config, batch, seq_len, device)
@@ -342,11 +381,11 @@ class _GraphedStack:
             self.kv_len.fill_(seq_len)
             self.row_mask.fill_(1)
         # One eager pass (first use of each kernel sets its attributes outside capture), then capture.
-        model._blocks(self.ws, batch, seq_len, self.kv_len, self.row_mask, packed)
+        model._blocks(self.ws, batch, seq_len, self.kv_len, self.row_mask, packed, fused)
         torch.cuda.current_stream(device).synchronize()
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
-            model._blocks(self.ws, batch, seq_len, self.kv_len, self.row_mask, packed)
+            model._blocks(self.ws, batch, seq_len, self.kv_len, self.row_mask, packed, fused)
 
     def run(self, x2: torch.Tensor, kv_len, row_mask, out2: torch.Tensor) -> None:
         if self.kv_len is not None:
