@@ -74,8 +74,8 @@ def parse_args(argv=None):
                    help="tensor-parallel reduction: reduce-scatter in the GEMMs + all-gather in the LayerNorm over "
                         "NVLink (rs), or NCCL all-reduce")
     p.add_argument("--fuse-ln", default="auto", choices=("auto", "on", "off"),
-                   help="LayerNorm inside the out_proj / ffn_out GEMM epilogues (auto: where the fused launch keeps "
-                        "the plain GEMM's one-CTA tiles)")
+                   help="LayerNorm inside the out_proj / ffn_out GEMM epilogues (auto: where the library recommends "
+                        "it; nowhere in this build, it measured slower than the separate LayerNorm)")
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
     p.add_argument("--cpu-seconds", type=float, default=15.0, help="target CPU time of the CPU baseline sample")
     return p.parse_args(argv)

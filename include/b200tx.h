@@ -118,8 +118,9 @@ int b2_linear_ln_fwd(const void* a, const void* w, const void* bias, int64_t m, 
  * The tile b2_linear_ln_fwd uses for n output columns (no device work): returns 0 and sets *tile_n
  * and *cluster (CTAs per 128-row stripe; n <= 256: one CTA, else a power-of-two cluster first,
  * then the widest tile), and *recommended = 1 where the fused launch is expected to beat
- * b2_linear_fwd + b2_layernorm_fwd. The plan depends on n only, so a row's output never depends on
- * m (batch shards reproduce the full batch bit for bit). Returns 2 when n has no plan. m and k are
+ * b2_linear_fwd + b2_layernorm_fwd (0 for every n in this build: measured slower on B200 at the
+ * benchmark sizes). The plan depends on n only, so a row's output never depends on m (batch shards
+ * reproduce the full batch bit for bit). Returns 2 when n has no plan. m and k are
  * validated only; sm_count is unused (kept for the signature).
  */
 int b2_linear_ln_plan(int64_t m, int64_t n, int64_t k, int sm_count, int* tile_n, int* cluster, int* recommended);

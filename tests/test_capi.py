@@ -72,11 +72,11 @@ def test_layernorm_rejects_bad_arguments(lib):
 
 def test_linear_ln_plan_depends_on_n_only(lib):
     for m in (1, 4096, 100000):
-        assert _capi.linear_ln_plan(m, 768, 768, sm_count=148) == (192, 4, True)
+        assert _capi.linear_ln_plan(m, 768, 768, sm_count=148) == (192, 4, False)
     assert _capi.linear_ln_plan(4096, 1024, 4096, sm_count=148) == (256, 4, False)
     assert _capi.linear_ln_plan(4096, 2048, 8192, sm_count=148) == (256, 8, False)
-    assert _capi.linear_ln_plan(64, 96, 64, sm_count=148) == (128, 1, True)
-    assert _capi.linear_ln_plan(64, 640, 64, sm_count=148) == (128, 5, True)
+    assert _capi.linear_ln_plan(64, 96, 64, sm_count=148) == (128, 1, False)
+    assert _capi.linear_ln_plan(64, 640, 64, sm_count=148) == (128, 5, False)
     assert _capi.linear_ln_plan(64, 2560, 64, sm_count=148) is None  # 10 CTAs per row
     assert _capi.linear_ln_plan(64, 48, 64, sm_count=148) is None
 

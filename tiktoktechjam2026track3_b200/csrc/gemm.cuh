@@ -18,11 +18,13 @@
 //   kEpiResidualLn      kEpiResidual, then ln_out_bf16 = LayerNorm(res_f32 row)        (out_proj + norm2)
 //   kEpiResidualZeroLn  kEpiResidualZero, then ln_out_bf16 = LayerNorm(res_f32 row)    (ffn_out + next norm1)
 // The two *Ln epilogues need whole rows: they run as clusters of N / BN CTAs, CTA r of a cluster
-// computing column block r of the same 128 rows, and exchange per-row partial sums through
-// distributed shared memory (two rounds: the sum, then the sum of squared deviations from the
-// mean, as nn.LayerNorm's biased variance; every CTA adds the partials in the same fixed order,
-// so all of them normalise a row with bit-identical statistics). The residual tile is written
-// back into the TMEM accumulator between the rounds, so it is read from HBM once.
+// computing column block r of the same 128 rows. Each epilogue warp reduces its rows' values to
+// (mean, sum of squared deviations) pairs, merges them pairwise (Chan et al.'s update for
+// combining variances), and sends them to every CTA of the cluster through distributed shared
+// memory in one exchange; every CTA merges the pairs in the same fixed order, so all of them
+// normalise a row with bit-identical statistics (nn.LayerNorm's biased variance). The updated
+// residual waits in the TMEM accumulator during the exchange; it is read from HBM once and
+// written once, after the exchange, together with the LayerNorm output.
 // A is [M, K] row-major bf16 (tokens x features), W is [N, K] row-major bf16 (nn.Linear layout,
 // i.e. K-major for the B operand), the residual stream is fp32 [M, ldo].
 //
@@ -103,11 +105,16 @@ __host__ __device__ constexpr bool is_ln_epi() {
   return EPI == kEpiResidualLn || EPI == kEpiResidualZeroLn;
 }
 
-// Row-statistics exchange of the *Ln epilogues: 8 mbarriers (2 rounds x 4 TMEM lane quadrants)
-// and the partial sums [round][quadrant][source = 2 * cluster rank + column half][32 rows].
+// Row-statistics exchange of the *Ln epilogues: 8 mbarriers [tile parity][TMEM lane quadrant] and
+// the (mean, M2) pairs [tile parity][quadrant][source = 2 * cluster rank + column half][32 rows].
+// Senders write with st.async, which counts the bytes on the receiver's barrier; each barrier is
+// armed (expect_tx of all 2 * cs * 256 bytes) before any sender can write its phase: at launch
+// for the first two tiles, and by the receiver right after it has read a phase's pairs for the
+// phase two tiles later. No CTA gets two tiles ahead of another (that needs the slow CTA's pairs),
+// so the two parities keep tile t+1's pairs off the slots and the barrier of tile t.
 constexpr int kLnMaxCluster = 8;
 constexpr int kLnBarrierBytes = 128;
-constexpr int kLnBytes = kLnBarrierBytes + 2 * 4 * (2 * kLnMaxCluster) * 32 * 4;
+constexpr int kLnBytes = kLnBarrierBytes + 2 * 4 * (2 * kLnMaxCluster) * 32 * 8;
 
 // Epilogue staging: TMEM gives each lane one row of the accumulator, so a lane writing its own
 // row would make every warp-wide global access touch 32 different rows (32 memory transactions
@@ -220,13 +227,16 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmParams& p, int row
 }
 
 // Pass 1 of the *Ln epilogues for one warp's 32 rows x 32 columns (layout as in
-// gemm_epilogue_chunk): updates and stores the fp32 residual, returns the updated values in
-// `vals` (lane i: rows 4j + i / 8, columns 4(i % 8) .. +3, j = 0..7, as vals[4j .. 4j+3]) and adds
-// each row's 4 values to part[j]. Masked rows keep their residual (kEpiResidualLn) or become 0
-// (kEpiResidualZeroLn); either way they are normalised like the others, as nn.LayerNorm does.
+// gemm_epilogue_chunk): the updated residual values come back in `vals` (lane i: rows 4j + i / 8,
+// columns 4(i % 8) .. +3, j = 0..7, as vals[4j .. 4j+3]); nothing is stored yet. Per row j the
+// lane accumulates sum[j] and sq[j] = sum of (x - shift[j])^2, shift[j] being its first value of
+// the row (so the variance does not cancel when the mean is large). Bit j of keep_bits / live_bits:
+// the row is kept by the mask / inside M. Masked rows keep their residual (kEpiResidualLn) or
+// become 0 (kEpiResidualZeroLn); either way they are normalised like the others, as nn.LayerNorm does.
 template <int EPI>
 __device__ __forceinline__ void gemm_ln_chunk(const GemmParams& p, int row0, int col0, float (&vals)[32],
-                                              float4* stage, float (&part)[8]) {
+                                              float4* stage, bool first, float (&sum)[8], float (&sq)[8],
+                                              float (&shift)[8], uint32_t& keep_bits, uint32_t& live_bits) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int c = 0; c < 8; ++c)
@@ -254,7 +264,6 @@ __device__ __forceinline__ void gemm_ln_chunk(const GemmParams& p, int row0, int
   }
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const int64_t off = static_cast<int64_t>(row0 + i * 4 + (lane >> 3)) * p.ldo + col;
     float4 o = res[i];
     if (keep[i]) {
       o.x += v[i].x + b.x;
@@ -262,56 +271,136 @@ __device__ __forceinline__ void gemm_ln_chunk(const GemmParams& p, int row0, int
       o.z += v[i].z + b.z;
       o.w += v[i].w + b.w;
     }
-    if (keep[i] || (EPI == kEpiResidualZeroLn && live[i])) *reinterpret_cast<float4*>(static_cast<float*>(p.out) + off) = o;
+    keep_bits |= keep[i] ? (1u << i) : 0u;
+    live_bits |= live[i] ? (1u << i) : 0u;
     vals[4 * i] = o.x;
     vals[4 * i + 1] = o.y;
     vals[4 * i + 2] = o.z;
     vals[4 * i + 3] = o.w;
-    part[i] += (o.x + o.y) + (o.z + o.w);
+    if (first) shift[i] = o.x;
+    sum[i] += (o.x + o.y) + (o.z + o.w);
+    const float dx = o.x - shift[i], dy = o.y - shift[i], dz = o.z - shift[i], dw = o.w - shift[i];
+    sq[i] = fmaf(dw, dw, fmaf(dz, dz, fmaf(dy, dy, fmaf(dx, dx, sq[i]))));
   }
   __syncwarp();
 }
 
-// Completes one round of the *Ln row statistics: part[j] holds this lane's partial sum for row
-// 4j + lane / 8 of the warp's 32 rows (over its columns of this CTA's tile). Sums it over the 8
-// lanes of the row, over the two column halves of the quadrant and over the cluster's CTAs, and
-// returns the row totals in tot[j] (identical bits in every CTA: fixed summation order). Returns
-// false when the wait for the other CTAs gave up (status recorded, *abort raised).
-__device__ __forceinline__ bool gemm_ln_allreduce(float (&part)[8], float (&tot)[8], int round, int quad, int half,
-                                                  uint32_t parity, int cs, uint32_t my_rank, uint64_t* xbar,
-                                                  float* xch, volatile int* abort) {
+// Turns this lane's per-row (sum, sq, shift) over n_lane values into the row's (mean, M2) over
+// the warp's columns, merged across the 8 lanes of each row (equal counts; the merge is symmetric
+// in its operands, so every lane of a row ends with the same bits), sends row `lane`'s pair to
+// every CTA of the cluster, waits for the cluster's pairs and merges all 2 * cs of them in source
+// order into mean[j] and rstd[j] for the lane's rows 4j + lane / 8. Returns false when the wait
+// gave up (status recorded, *abort raised).
+__device__ __forceinline__ bool gemm_ln_stats(const GemmParams& p, int bn, float n_lane, const float (&sum)[8],
+                                              const float (&sq)[8], const float (&shift)[8], float (&mean)[8],
+                                              float (&rstd)[8], int quad, int half, uint32_t parity,
+                                              uint32_t use_parity, uint32_t my_rank, uint64_t* xbar, float* xch,
+                                              volatile int* abort) {
   const int lane = threadIdx.x & 31;
+  const int cs = p.n_blocks;
+  float m2[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    part[j] += __shfl_xor_sync(0xffffffffu, part[j], 1);
-    part[j] += __shfl_xor_sync(0xffffffffu, part[j], 2);
-    part[j] += __shfl_xor_sync(0xffffffffu, part[j], 4);
+    if (n_lane > 0.f) {
+      mean[j] = sum[j] / n_lane;
+      const float d = mean[j] - shift[j];
+      m2[j] = fmaxf(sq[j] - n_lane * d * d, 0.f);
+    } else {
+      mean[j] = 0.f;
+      m2[j] = 0.f;
+    }
+  }
+  float n = n_lane;
+#pragma unroll
+  for (int o = 1; o <= 4; o <<= 1) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float mb = __shfl_xor_sync(0xffffffffu, mean[j], o);
+      const float qb = __shfl_xor_sync(0xffffffffu, m2[j], o);
+      const float d = mb - mean[j];
+      m2[j] = (m2[j] + qb) + d * d * (0.5f * n);
+      mean[j] = (mean[j] + mb) * 0.5f;
+    }
+    n *= 2.f;
   }
   // Lane L takes row L: row 4j + g is held by the lanes 8g .. 8g+7, j = L / 4, g = L % 4.
-  float mine = 0.f;
+  float my_mean = 0.f, my_m2 = 0.f;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    const float t = __shfl_sync(0xffffffffu, part[j], (lane & 3) << 3);
-    if ((lane >> 2) == j) mine = t;
+    const float tm = __shfl_sync(0xffffffffu, mean[j], (lane & 3) << 3);
+    const float tq = __shfl_sync(0xffffffffu, m2[j], (lane & 3) << 3);
+    if ((lane >> 2) == j) {
+      my_mean = tm;
+      my_m2 = tq;
+    }
   }
-  float* block = xch + (round * 4 + quad) * (2 * kLnMaxCluster) * 32;
-  uint64_t* bar = &xbar[round * 4 + quad];
-  const uint32_t slot = smem_u32(block + (2 * static_cast<int>(my_rank) + half) * 32 + lane);
+  float* block = xch + ((parity * 4 + quad) * (2 * kLnMaxCluster)) * 32 * 2;
+  const uint32_t slot = smem_u32(block + ((2 * static_cast<int>(my_rank) + half) * 32 + lane) * 2);
+  uint64_t* bar = &xbar[parity * 4 + quad];
   for (int r = 0; r < cs; ++r) {
     uint32_t dst, dbar;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(dst) : "r"(slot), "r"(r));
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(dbar) : "r"(smem_u32(bar)), "r"(r));
-    st_cluster_f32(dst, mine);
-    mbar_arrive_cluster(dbar);  // release: orders the store above before the arrival
+    st_async_v2f32(dst, my_mean, my_m2, dbar);
   }
-  if (!mbar_wait_cluster(bar, parity, abort, kKernelGemm, 6 + round)) return false;
+  // One lane polls (test_wait: no suspension), the warp then re-converges and reads: with all 32
+  // lanes in a suspending try_wait, lanes woke up microseconds after the bytes had landed.
+  bool ok = true;
+  if (lane == 0 && !mbar_test_wait_cluster(bar, use_parity)) {
+    const uint64_t t0 = global_timer_ns();
+    uint32_t spins = 0;
+    while (!mbar_test_wait_cluster(bar, use_parity)) {
+      if ((++spins & 63u) == 0) {
+        if (*abort) {
+          ok = false;
+          break;
+        }
+        if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+          record_status(kKernelGemm, 6, kReasonTimeout);
+          *abort = 1;
+          ok = false;
+          break;
+        }
+      }
+    }
+  }
+  if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) return false;
+  // Sources outer, the lane's 8 rows inner: 8 independent accumulation chains per step. Every
+  // source holds bn / 2 columns except, in a single-CTA row (n <= 256), a half past n.
+  const float inv_n = 1.0f / static_cast<float>(p.N);
+  const float2* pairs = reinterpret_cast<const float2*>(block) + (lane >> 3);
+  const int n_src = cs == 1 ? (p.N > bn / 2 ? 2 : 1) : 2 * cs;
+  const float w_last = static_cast<float>(cs == 1 ? p.N - (n_src - 1) * (bn / 2) : bn / 2);
+  const float w_full = static_cast<float>(bn / 2);
+  float tot[8], m2t[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    const float* rowp = block + j * 4 + (lane >> 3);
-    float t = 0.f;
-    for (int src = 0; src < 2 * cs; ++src) t += rowp[src * 32];
-    tot[j] = t;
+    tot[j] = 0.f;
+    m2t[j] = 0.f;
   }
+  for (int src = 0; src < n_src; ++src) {
+    const float w = src == n_src - 1 ? w_last : w_full;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) tot[j] = fmaf(w, pairs[src * 32 + j * 4].x, tot[j]);
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) mean[j] = tot[j] * inv_n;
+  for (int src = 0; src < n_src; ++src) {
+    const float w = src == n_src - 1 ? w_last : w_full;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float2 pr = pairs[src * 32 + j * 4];
+      const float d = pr.x - mean[j];
+      m2t[j] += pr.y + w * d * d;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) rstd[j] = rsqrtf(m2t[j] * inv_n + p.ln_eps);
+  // Re-arm this barrier for its next phase (tile t+2). Both warps of the quadrant have seen this
+  // phase complete or will (the next one needs their own bytes); the pairs just read cannot be
+  // overwritten before then (a sender must first receive this CTA's pairs of tile t+1).
+  __syncwarp();
+  if (half == 0 && lane == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(2 * cs * 32 * 8));
   return true;
 }
 
@@ -359,8 +448,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if constexpr (is_ln_epi<EPI>()) {
       uint64_t* xbar = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(full) + Cfg::kBarrierBytes +
                                                    kEpiStageBytes);
-      // Every quadrant warp (2 per CTA) of every CTA of the cluster arrives once per lane.
-      for (int i = 0; i < 8; ++i) mbar_init(&xbar[i], 2 * p.n_blocks * 32);
+      // One local arrival per phase (the arming expect_tx); the bytes of all 2 * cs source warps
+      // complete it. Both parities are armed here, before the cluster barrier lets anyone send.
+      for (int i = 0; i < 8; ++i) {
+        mbar_init(&xbar[i], 1);
+        mbar_arrive_expect_tx(&xbar[i], static_cast<uint32_t>(2 * p.n_blocks * 32 * 8));
+      }
     }
     fence_mbarrier_init();
   }
@@ -483,68 +576,77 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t t_row =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * Cfg::kAccStride);
       if constexpr (is_ln_epi<EPI>()) {
-        // Round 1: residual update, stored to HBM and written back over the accumulator; row sums.
+        constexpr int kChunks = BN / 64;  // 32-column chunks per warp (one half of the tile)
         uint64_t* xbar = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(full) + Cfg::kBarrierBytes +
                                                      kEpiStageBytes);
         float* xch = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xbar) + kLnBarrierBytes);
         const uint32_t my_rank = static_cast<uint32_t>(n_blk);  // == %cluster_ctarank
-        const uint32_t parity = static_cast<uint32_t>(local & 1);
-        const float inv_d = 1.0f / static_cast<float>(p.N);
-        float part[8], mean[8], rstd[8];
+        const int c_first = half * kChunks;
+        // gamma / beta of this lane's columns, loaded before the main work hides their latency.
+        float4 g[kChunks], bt[kChunks];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) part[j] = 0.f;
+        for (int c = 0; c < kChunks; ++c) {
+          const int col = n_blk * BN + (c_first + c) * 32 + 4 * (lane & 7);
+          g[c] = col < p.N ? load_bias4(p.ln_gamma, col) : make_float4(0.f, 0.f, 0.f, 0.f);
+          bt[c] = col < p.N ? load_bias4(p.ln_beta, col) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        // Pass 1: residual update into TMEM (over the consumed accumulator), row statistics.
+        float sum[8], sq[8], shift[8], mean[8], rstd[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          sum[j] = 0.f;
+          sq[j] = 0.f;
+          shift[j] = 0.f;
+        }
+        uint32_t keep_bits = 0, live_bits = 0;
+        int chunks = 0;
 #pragma unroll 1
-        for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+        for (int c = c_first; c < c_first + kChunks; ++c) {
           const int col0 = n_blk * BN + c * 32;
           if (col0 >= p.N) break;  // warp-uniform
           float v[32];
           tmem_load_32cols(t_row + c * 32, v);
-          gemm_ln_chunk<EPI>(p, row - lane, col0, v, epi_stage, part);
-          tmem_store_32cols(t_row + c * 32, v);
+          gemm_ln_chunk<EPI>(p, row - lane, col0, v, epi_stage, c == c_first, sum, sq, shift, keep_bits, live_bits);
+          tmem_store_32cols_async(t_row + c * 32, v);
+          ++chunks;
         }
-        if (!gemm_ln_allreduce(part, mean, 0, quad, half, parity, p.n_blocks, my_rank, xbar, xch, abort_flag)) break;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          mean[j] *= inv_d;
-          part[j] = 0.f;
-        }
-        // Round 2: sum of squared deviations.
-#pragma unroll 1
-        for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
-          if (n_blk * BN + c * 32 >= p.N) break;
-          float v[32];
-          tmem_load_32cols(t_row + c * 32, v);
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float d = v[4 * j + e] - mean[j];
-              part[j] = fmaf(d, d, part[j]);
-            }
-        }
-        if (!gemm_ln_allreduce(part, rstd, 1, quad, half, parity, p.n_blocks, my_rank, xbar, xch, abort_flag)) break;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) rstd[j] = rsqrtf(rstd[j] * inv_d + p.ln_eps);
-        // Normalise: y = (x - mean) * rstd * gamma + beta, bf16, row segments of 8 lanes x 4 columns.
-#pragma unroll 1
-        for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
-          const int col0 = n_blk * BN + c * 32;
-          if (col0 >= p.N) break;
-          float v[32];
-          tmem_load_32cols(t_row + c * 32, v);
-          const int col = col0 + 4 * (lane & 7);
-          const float4 g = load_bias4(p.ln_gamma, col);
-          const float4 bt = load_bias4(p.ln_beta, col);
+        tmem_wait_st();
+        if (!gemm_ln_stats(p, BN, 4.0f * static_cast<float>(chunks), sum, sq, shift, mean, rstd, quad, half,
+                           static_cast<uint32_t>(local & 1), static_cast<uint32_t>((local >> 1) & 1), my_rank, xbar,
+                           xch, abort_flag))
+          break;
+        // Pass 3: store the residual (kept rows; masked rows too when they become 0) and the
+        // LayerNorm output, y = (x - mean) * rstd * gamma + beta, as 8-lane row segments. Two
+        // chunks per TMEM load where both exist (one load latency instead of two).
+        auto finish_chunk = [&](int c, const float* v) {
+          const int col = n_blk * BN + (c_first + c) * 32 + 4 * (lane & 7);
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const int r = row - lane + j * 4 + (lane >> 3);
-            if (r >= p.M) continue;
-            const float y0 = fmaf((v[4 * j] - mean[j]) * rstd[j], g.x, bt.x);
-            const float y1 = fmaf((v[4 * j + 1] - mean[j]) * rstd[j], g.y, bt.y);
-            const float y2 = fmaf((v[4 * j + 2] - mean[j]) * rstd[j], g.z, bt.z);
-            const float y3 = fmaf((v[4 * j + 3] - mean[j]) * rstd[j], g.w, bt.w);
-            *reinterpret_cast<uint2*>(p.ln_out + static_cast<int64_t>(r) * p.N + col) =
-                make_uint2(pack_bf16x2(y0, y1), pack_bf16x2(y2, y3));
+            if (!((live_bits >> j) & 1u)) continue;
+            const int64_t r = row - lane + j * 4 + (lane >> 3);
+            if (((keep_bits >> j) & 1u) || EPI == kEpiResidualZeroLn)
+              *reinterpret_cast<float4*>(static_cast<float*>(p.out) + r * p.ldo + col) =
+                  make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            const float y0 = fmaf((v[4 * j] - mean[j]) * rstd[j], g[c].x, bt[c].x);
+            const float y1 = fmaf((v[4 * j + 1] - mean[j]) * rstd[j], g[c].y, bt[c].y);
+            const float y2 = fmaf((v[4 * j + 2] - mean[j]) * rstd[j], g[c].z, bt[c].z);
+            const float y3 = fmaf((v[4 * j + 3] - mean[j]) * rstd[j], g[c].w, bt[c].w);
+            *reinterpret_cast<uint2*>(p.ln_out + r * p.N + col) = make_uint2(pack_bf16x2(y0, y1), pack_bf16x2(y2, y3));
+          }
+        };
+#pragma unroll
+        for (int c = 0; c < kChunks; c += 2) {
+          const int col0 = n_blk * BN + (c_first + c) * 32;
+          if (col0 >= p.N) break;  // warp-uniform
+          if (c + 1 < kChunks && col0 + 32 < p.N) {
+            float v[64];
+            tmem_load_64cols(t_row + (c_first + c) * 32, v);
+            finish_chunk(c, v);
+            finish_chunk(c + 1, v + 32);
+          } else {
+            float v[32];
+            tmem_load_32cols(t_row + (c_first + c) * 32, v);
+            finish_chunk(c, v);
           }
         }
       } else {
@@ -563,6 +665,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if constexpr (is_rs_epi<EPI>() || EPI == kEpiBiasPeers) fence_acq_rel_sys();
   }
 
+  if (is_ln_epi<EPI>() && *abort_flag && threadIdx.x == 0) {
+    // A wait gave up: give row-statistics stores still in flight to or from this CTA time to land.
+    const uint64_t t0 = global_timer_ns();
+    while (global_timer_ns() - t0 < 200000ull) {
+    }
+  }
   __syncthreads();
   if constexpr (is_ln_epi<EPI>()) cluster_sync_all();  // no CTA leaves while others may still write to it
   if (warp == 1) {
@@ -949,9 +1057,13 @@ cudaError_t launch_gemm(const __nv_bfloat16* A, const __nv_bfloat16* W, const __
 // CTAs) and each row's statistics are summed in an order fixed by bn, so the choice depends on N
 // alone — never on M — to keep every row's output independent of how many rows share the launch
 // (batch shards give the same bits as the full batch): n <= 256 takes one CTA; otherwise a
-// power-of-two cluster is preferred, then the widest tile. *recommended is 1 where the fused
-// launch is expected to beat GEMM + separate LayerNorm: everywhere but the 256-wide tiles of wide
-// rows, whose shared memory (LayerNorm exchange + epilogue staging) leaves a 3-deep operand ring.
+// power-of-two cluster is preferred, then the widest tile. *recommended is 0 for every width: on
+// B200 the fused launch measured slower than the GEMM followed by the separate LayerNorm kernel
+// (C2 1.668 vs 1.637 ms per forward, C3 4.70 vs 4.46, C1 0.228 vs 0.198). Its epilogue runs its
+// passes back to back on one 128-row tile per CTA (load and update the residual, merge and exchange
+// the row statistics, store residual and LayerNorm rows: 4.7 + 3.3 + 2.4 us at C2's out_proj), while
+// the separate LayerNorm, launched with programmatic dependent launch, overlaps the GEMM's tail and
+// adds about 3 us; with 256-wide tiles the exchange and staging buffers also leave a 3-deep ring.
 bool gemm_ln_plan(int64_t M, int64_t N, int64_t K, int sms, int* bn_out, int* cs_out, int* recommended) {
   (void)sms;
   if (M <= 0 || N <= 0 || K <= 0 || N % 32 != 0) return false;
@@ -974,7 +1086,7 @@ bool gemm_ln_plan(int64_t M, int64_t N, int64_t K, int sms, int* bn_out, int* cs
   }
   if (bn_out) *bn_out = bn;
   if (cs_out) *cs_out = cs;
-  if (recommended) *recommended = (bn != 256 || cs == 1) ? 1 : 0;
+  if (recommended) *recommended = 0;
   return true;
 }
 

@@ -171,7 +171,8 @@ class UserOptimizedTransformer(nn.Module):
         self.use_cuda_graph = True
         self._graphs: Dict[tuple, "_GraphedStack"] = {}
         # LayerNorm fused into the residual GEMMs (b2_linear_ln_fwd): "auto" where the library
-        # recommends it for d_model, True / False to force it on (where d_model has a plan) or off.
+        # recommends it for d_model (nowhere in this build: the fused launch measured slower than
+        # GEMM + LayerNorm on B200), True / False to force it on (where d_model has a plan) or off.
         # The choice depends on the model's widths only, never on the token count, so a batch shard
         # computes its rows exactly as the full batch does.
         self.fuse_layernorm = "auto"
