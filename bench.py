@@ -58,7 +58,7 @@ LONG_STEP_MS = 50.0
 # DRAM bytes (read + write) per launch of the dominant kernel class, averaged over the class's
 # launches in one forward, from an ncu capture of this bench (profiles/launches_bench_c2.md):
 # key = (workload, tensor-parallel ranks, kernel class, LayerNorm fused into the residual GEMMs).
-DRAM_BYTES_PER_LAUNCH = {("c2", 1, "gemm_tc_kernel", False): 19221899.5}
+DRAM_BYTES_PER_LAUNCH = {("c2", 1, "gemm_tc_kernel", False): 19224147.2}
 
 
 def parse_args(argv=None):
