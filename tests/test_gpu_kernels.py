@@ -204,6 +204,10 @@ ATTN_CASES = [
     (2, 300, 2, 128, False, [300, 129]),
     (1, 4096, 2, 128, True, None),
     (1, 384, 1, 128, False, None),
+    # enough CTAs that the tensor-core kernel keeps two query tiles per CTA (the small cases above
+    # fit one wave either way and run one tile per CTA): even and odd tile counts
+    (8, 1024, 16, 64, True, None),
+    (4, 1152, 16, 128, False, [1152, 1000, 640, 129]),
     # CUDA-core kernel (head dims of the reference's official case matrix)
     (2, 128, 4, 32, True, None),
     (3, 200, 4, 8, False, [200, 77, 1]),
@@ -267,21 +271,22 @@ def test_attention_query_row_range_matches_full(hd, causal, q_begin, q_count):
     assert torch.all(part[:, :q_begin] == 7.0) and torch.all(part[:, q_begin + q_count:] == 7.0)
 
 
-@pytest.mark.parametrize("hd", [64, 128, 32])
-def test_attention_two_query_ranges_match_full(hd):
-    """Two ranges in one launch (the context-parallel zigzag chunks) equal the full run on their rows."""
-    batch, seq, heads = 1, 2048, 2
+@pytest.mark.parametrize("hd,heads,n", [(64, 2, 256), (128, 2, 256), (32, 2, 256), (64, 64, 512)])
+def test_attention_two_query_ranges_match_full(hd, heads, n):
+    """Two ranges in one launch (the context-parallel zigzag chunks) equal the full run on their rows
+    (64 heads x 2 x 4 query tiles: enough CTAs for two query tiles per CTA)."""
+    batch, seq = 1, 2048
     d = heads * hd
     g = _gen(11 + hd)
     qkv = torch.randn(batch * seq, 3 * d, device="cuda", generator=g).bfloat16()
     full = torch.zeros(seq, d, device="cuda", dtype=torch.bfloat16)
     part = torch.full((seq, d), 7.0, device="cuda", dtype=torch.bfloat16)
+    ranges = [(256, n), (1536, n)]
     _capi.attention(qkv, batch, seq, heads, hd, 0, d, 2 * d, None, True, hd**-0.5, full)
-    _capi.attention(qkv, batch, seq, heads, hd, 0, d, 2 * d, None, True, hd**-0.5, part,
-                    q_rows=[(256, 256), (1536, 256)])
-    for r0, n in [(256, 256), (1536, 256)]:
-        assert torch.equal(part[r0:r0 + n], full[r0:r0 + n])
-    assert torch.all(part[:256] == 7.0) and torch.all(part[512:1536] == 7.0) and torch.all(part[1792:] == 7.0)
+    _capi.attention(qkv, batch, seq, heads, hd, 0, d, 2 * d, None, True, hd**-0.5, part, q_rows=ranges)
+    for r0, cnt in ranges:
+        assert torch.equal(part[r0:r0 + cnt], full[r0:r0 + cnt])
+    assert torch.all(part[:256] == 7.0) and torch.all(part[256 + n:1536] == 7.0) and torch.all(part[1536 + n:] == 7.0)
 
 
 def test_attention_reads_heads_at_column_offsets():

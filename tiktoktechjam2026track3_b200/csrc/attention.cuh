@@ -38,6 +38,9 @@ struct AttnParams {
   int q_tile0[2];    // first query tile (128 rows) of the range
   int n_q_tiles[2];  // query tiles in the range
   int q_end[2];      // one past the last query row of the range
+  // Query tiles per CTA of the tensor-core kernel: 2 (one per softmax group) or 1 (group 1 idle),
+  // chosen at launch by the wave count (attention_pair_tiles_per_cta).
+  int tiles_per_cta;
 };
 
 // Query range of the CTA row `y` of a grid whose rows cover `per_range[r]` work items of range r,
@@ -93,6 +96,7 @@ cudaError_t launch_attention(const __nv_bfloat16* qkv, int64_t ld_qkv, int64_t q
   p.causal = causal;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.n_ranges = n_ranges;
+  p.tiles_per_cta = 2;
   for (int r = 0; r < 2; ++r) {
     const int64_t q_begin = r < n_ranges ? q_ranges[2 * r] : 0;
     const int64_t q_count = r < n_ranges ? q_ranges[2 * r + 1] : 0;

@@ -12,7 +12,8 @@
 // group's exponentials run while the other group waits, and the tensor core alternates between
 // the groups.
 //
-// CTA = (b, h, query-tile pair c), 12 warps at head_dim 64, 11 at head_dim 128:
+// CTA = (b, h, query-tile pair c), 12 warps at head_dim 64, 11 at head_dim 128 (or, where that
+// fills the SMs better, one query tile per CTA with group 1 idle; attention_pair_tiles_per_cta):
 //   warp 0      TMA: Q tiles 2c, 2c+1 once; K_j and V_j (128 keys) into two independent 4-stage
 //               rings, each refilled as soon as its own slot frees (K never waits behind V).
 //   warps 1, 2  UMMA issuers, one per softmax group (warp 1 also allocates TMEM). tcgen05.mma
@@ -124,7 +125,8 @@ __global__ void __launch_bounds__(AttnPairCfg<HD>::kThreads, 1)
   const int lane = threadIdx.x & 31;
   const int b = blockIdx.x / p.H;
   const int h = blockIdx.x % p.H;
-  const int range_pairs[2] = {(p.n_q_tiles[0] + 1) >> 1, (p.n_q_tiles[1] + 1) >> 1};
+  const int tpc = p.tiles_per_cta;  // query tiles per CTA: 2, or 1 with group 1 idle
+  const int range_pairs[2] = {(p.n_q_tiles[0] + tpc - 1) / tpc, (p.n_q_tiles[1] + tpc - 1) / tpc};
   int y_local;
   const int rg = attn_range_of(p, static_cast<int>(blockIdx.y), range_pairs, y_local);
   const int pair = range_pairs[rg] - 1 - y_local;  // heaviest causal pairs first
@@ -135,14 +137,14 @@ __global__ void __launch_bounds__(AttnPairCfg<HD>::kThreads, 1)
   int n_kv[2];
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
-    const int qt = q_tile0 + 2 * pair + t;  // absolute query tile
-    const bool live = 2 * pair + t < p.n_q_tiles[rg] && qt * 128 < kv_len;
+    const int qt = q_tile0 + tpc * pair + t;  // absolute query tile
+    const bool live = t < tpc && tpc * pair + t < p.n_q_tiles[rg] && qt * 128 < kv_len;
     n_kv[t] = live ? (p.causal ? min(qt + 1, kv_tiles) : kv_tiles) : 0;
   }
   const int n_total = max(n_kv[0], n_kv[1]);
   if (n_total == 0) return;  // uniform for the CTA: nothing allocated yet
   const int row_base = b * p.S;
-  const int q_row0 = row_base + (q_tile0 + 2 * pair) * 128;
+  const int q_row0 = row_base + (q_tile0 + tpc * pair) * 128;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -185,11 +187,12 @@ __global__ void __launch_bounds__(AttnPairCfg<HD>::kThreads, 1)
       const int qc = p.q_col + h * HD;
       const int kc = p.k_col + h * HD;
       const int vc = p.v_col + h * HD;
-      mbar_arrive_expect_tx(q_full, 2 * Cfg::kQBytes);
+      mbar_arrive_expect_tx(q_full, static_cast<uint32_t>(tpc * Cfg::kQBytes));
 #pragma unroll
       for (int c = 0; c < Cfg::kBoxes; ++c) {
         tma_load_2d(s_q + c * Cfg::kBoxBytes, &tm_qkv, q_full, qc + 64 * c, q_row0);
-        tma_load_2d(s_q + Cfg::kQBytes + c * Cfg::kBoxBytes, &tm_qkv, q_full, qc + 64 * c, q_row0 + 128);
+        if (tpc == 2)
+          tma_load_2d(s_q + Cfg::kQBytes + c * Cfg::kBoxBytes, &tm_qkv, q_full, qc + 64 * c, q_row0 + 128);
       }
       // K and V rings refill independently (polling both), so a K tile never waits for a V slot.
       int k_next = 0, v_next = 0;
@@ -350,7 +353,7 @@ __global__ void __launch_bounds__(AttnPairCfg<HD>::kThreads, 1)
     const int grp = (warp - Cfg::kSoftmaxWarp0) >> 2;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
-    const int qt = q_tile0 + 2 * pair + grp;
+    const int qt = q_tile0 + tpc * pair + grp;
     const int query = qt * 128 + r;
     const int n = grp == 0 ? n_kv[0] : n_kv[1];
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
@@ -502,6 +505,28 @@ __global__ void __launch_bounds__(AttnPairCfg<HD>::kThreads, 1)
   }
 }
 
+int device_sm_count(int device);
+
+// Query tiles per CTA. Two tiles (one per softmax group) share the exponential unit and the K/V
+// stream; a single-tile CTA (group 1 idle) takes about 0.75 of a pair CTA's time (measured on
+// B200: C2's attention, 192 pair CTAs in two waves 37.8 us, 384 single-tile CTAs in three waves
+// 42.4 us). Single-tile CTAs are chosen when their wave count times that factor beats the pair
+// waves — in practice when both fit the same number of waves, so the extra CTAs fill idle SMs
+// (B=1 S=1024 16 heads: 33.2 -> 29.9 us; B=2 S=512 head_dim 128: 30.2 -> 27.9 us).
+static int attention_pair_tiles_per_cta(const AttnParams& p, int sms) {
+  constexpr double kSingleCost = 0.75;  // single-tile CTA time / pair CTA time (same KV tiles)
+  long tiles = 0, pairs = 0;
+  for (int r = 0; r < p.n_ranges; ++r) {
+    tiles += p.n_q_tiles[r];
+    pairs += (p.n_q_tiles[r] + 1) / 2;
+  }
+  const long ctas2 = static_cast<long>(p.B) * p.H * pairs;
+  const long ctas1 = static_cast<long>(p.B) * p.H * tiles;
+  const long waves2 = (ctas2 + sms - 1) / sms;
+  const long waves1 = (ctas1 + sms - 1) / sms;
+  return kSingleCost * static_cast<double>(waves1) < static_cast<double>(waves2) ? 1 : 2;
+}
+
 template <int HD>
 static cudaError_t launch_attention_pair(const CUtensorMap& tm, const AttnParams& p, cudaStream_t stream) {
   using Cfg = AttnPairCfg<HD>;
@@ -514,8 +539,11 @@ static cudaError_t launch_attention_pair(const CUtensorMap& tm, const AttnParams
                                     Cfg::kSmemBytes);
   });
   if (attr_err != cudaSuccess) return attr_err;
-  dim3 grid(p.B * p.H, (p.n_q_tiles[0] + 1) / 2 + (p.n_ranges > 1 ? (p.n_q_tiles[1] + 1) / 2 : 0));
-  return launch_pdl(attention_pair_kernel<HD>, grid, dim3(Cfg::kThreads), Cfg::kSmemBytes, stream, tm, p);
+  AttnParams q = p;
+  q.tiles_per_cta = attention_pair_tiles_per_cta(p, device_sm_count(dev));
+  const int t = q.tiles_per_cta;
+  dim3 grid(p.B * p.H, (p.n_q_tiles[0] + t - 1) / t + (p.n_ranges > 1 ? (p.n_q_tiles[1] + t - 1) / t : 0));
+  return launch_pdl(attention_pair_kernel<HD>, grid, dim3(Cfg::kThreads), Cfg::kSmemBytes, stream, tm, q);
 }
 
 }  // namespace b2
