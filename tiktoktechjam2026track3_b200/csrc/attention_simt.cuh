@@ -5,10 +5,14 @@
 // online softmax in fp32, context written as bf16 into the token-major [B*S, H*hd] rows.
 //
 // Block = 128 threads over (b, h, a run of queries); TPQ = max(1, hd / 32) consecutive threads
-// share a query, each holding hd / TPQ (<= 32) of its dims of q and of the output in registers,
-// so a score is a TPQ-wide shuffle reduction of partial dot products. Keys and values stream
-// through shared memory in chunks of 64 keys (16-byte loads; the whole block shares a chunk).
-// The running maximum is per query; the output is rescaled only when it moves.
+// share a query, each holding hd / TPQ (<= 32) of its dims of q and of the output in registers
+// (4-dim groups interleaved over the TPQ threads, so their shared-memory reads of a key row are
+// consecutive 16-byte pieces, free of bank conflicts), so a score is a TPQ-wide shuffle reduction
+// of partial dot products. Keys and values stream through shared memory in chunks, converted to
+// fp32 once when staged (16-byte loads; the whole block shares a chunk), so the inner loop is
+// 16-byte broadcast loads and FMAs only — converting bf16 at every use cost as many instructions
+// as the FMAs. The running maximum is per query and, as in the tensor-core kernel, moves only
+// when a score exceeds it by more than 2^8 (exp2 units), which keeps the rescale branch rare.
 #pragma once
 #include "b2_common.cuh"
 
@@ -20,9 +24,9 @@ struct AttnSimtCfg {
   static constexpr int kTPQ = HD <= 32 ? 1 : HD / 32;  // threads per query
   static constexpr int kDPT = HD / kTPQ;               // dims per thread
   static constexpr int kQPB = kThreads / kTPQ;         // queries per block
-  static constexpr int kChunk = 64;                    // keys per shared-memory chunk
-  static constexpr int kSmemBytes = 2 * kChunk * HD * 2;
-  static_assert(HD % 8 == 0 && kDPT <= 32 && (kTPQ & (kTPQ - 1)) == 0, "head_dim");
+  static constexpr int kChunk = HD >= 256 ? 32 : 64;   // keys per shared-memory chunk
+  static constexpr int kSmemBytes = 2 * kChunk * HD * 4;  // fp32 K and V
+  static_assert(HD % 8 == 0 && kDPT <= 32 && kDPT % 4 == 0 && (kTPQ & (kTPQ - 1)) == 0, "head_dim");
 };
 
 template <int HD>
@@ -30,8 +34,8 @@ __global__ void __launch_bounds__(128) attention_simt_kernel(const __nv_bfloat16
                                                              AttnParams p) {
   using Cfg = AttnSimtCfg<HD>;
   extern __shared__ __align__(16) uint8_t simt_smem[];
-  __nv_bfloat16* sk = reinterpret_cast<__nv_bfloat16*>(simt_smem);
-  __nv_bfloat16* sv = sk + Cfg::kChunk * HD;
+  float* sk = reinterpret_cast<float*>(simt_smem);
+  float* sv = sk + Cfg::kChunk * HD;
   pdl_wait_previous_grid();
   pdl_allow_next_grid();
 
@@ -46,26 +50,27 @@ __global__ void __launch_bounds__(128) attention_simt_kernel(const __nv_bfloat16
   const int kv_len = p.kv_len != nullptr ? p.kv_len[b] : p.S;
   const int qi = q0 + static_cast<int>(threadIdx.x) / Cfg::kTPQ;
   const int sub = static_cast<int>(threadIdx.x) % Cfg::kTPQ;
-  const int d0 = sub * Cfg::kDPT;
+  // Float4 group i of this thread holds dims 4 (i TPQ + sub) .. +3.
+  auto dim_of = [&](int i) { return (i * Cfg::kTPQ + sub) * 4; };
   const int64_t row_base = static_cast<int64_t>(b) * p.S;
   const bool live = qi < q_end;
   const int limit = p.causal ? min(kv_len, qi + 1) : kv_len;
   // Keys the block needs: up to the last query's causal limit.
   const int q_last = min(q0 + Cfg::kQPB, q_end) - 1;
   const int block_keys = p.causal ? min(kv_len, q_last + 1) : kv_len;
+  constexpr float kRescaleThreshold = 8.0f;  // exp2 units
 
   float q[Cfg::kDPT], o[Cfg::kDPT];
   if (live) {
-    const __nv_bfloat16* qp = qkv + (row_base + qi) * ld_qkv + p.q_col + h * HD + d0;
+    const __nv_bfloat16* qp = qkv + (row_base + qi) * ld_qkv + p.q_col + h * HD;
 #pragma unroll
-    for (int i = 0; i < Cfg::kDPT; i += 8) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(qp + i);
+    for (int i = 0; i < Cfg::kDPT / 4; ++i) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(qp + dim_of(i));
       const __nv_bfloat162* hv = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        q[i + 2 * k] = __low2float(hv[k]) * p.scale_log2;
-        q[i + 2 * k + 1] = __high2float(hv[k]) * p.scale_log2;
-      }
+      q[4 * i] = __low2float(hv[0]) * p.scale_log2;
+      q[4 * i + 1] = __high2float(hv[0]) * p.scale_log2;
+      q[4 * i + 2] = __low2float(hv[1]) * p.scale_log2;
+      q[4 * i + 3] = __high2float(hv[1]) * p.scale_log2;
     }
   } else {
 #pragma unroll
@@ -83,23 +88,34 @@ __global__ void __launch_bounds__(128) attention_simt_kernel(const __nv_bfloat16
       const int key = idx / kVecPerRow;
       const int col = (idx % kVecPerRow) * 8;
       const __nv_bfloat16* base = qkv + (row_base + c0 + key) * ld_qkv + h * HD + col;
-      *reinterpret_cast<uint4*>(sk + key * HD + col) = *reinterpret_cast<const uint4*>(base + p.k_col);
-      *reinterpret_cast<uint4*>(sv + key * HD + col) = *reinterpret_cast<const uint4*>(base + p.v_col);
+      const uint4 kraw = *reinterpret_cast<const uint4*>(base + p.k_col);
+      const uint4 vraw = *reinterpret_cast<const uint4*>(base + p.v_col);
+      const __nv_bfloat162* kh = reinterpret_cast<const __nv_bfloat162*>(&kraw);
+      const __nv_bfloat162* vh = reinterpret_cast<const __nv_bfloat162*>(&vraw);
+      float4* kd = reinterpret_cast<float4*>(sk + key * HD + col);
+      float4* vd = reinterpret_cast<float4*>(sv + key * HD + col);
+      kd[0] = make_float4(__low2float(kh[0]), __high2float(kh[0]), __low2float(kh[1]), __high2float(kh[1]));
+      kd[1] = make_float4(__low2float(kh[2]), __high2float(kh[2]), __low2float(kh[3]), __high2float(kh[3]));
+      vd[0] = make_float4(__low2float(vh[0]), __high2float(vh[0]), __low2float(vh[1]), __high2float(vh[1]));
+      vd[1] = make_float4(__low2float(vh[2]), __high2float(vh[2]), __low2float(vh[3]), __high2float(vh[3]));
     }
     __syncthreads();
     for (int kk = 0; kk < n; ++kk) {
-      const __nv_bfloat16* kr = sk + kk * HD + d0;
-      float s = 0.f;
+      const float* kr = sk + kk * HD;
+      float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-      for (int i = 0; i < Cfg::kDPT; i += 2) {
-        const float2 kf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(kr + i));
-        s = fmaf(q[i], kf.x, s);
-        s = fmaf(q[i + 1], kf.y, s);
+      for (int i = 0; i < Cfg::kDPT / 4; ++i) {
+        const float4 kf = *reinterpret_cast<const float4*>(kr + dim_of(i));
+        s0 = fmaf(q[4 * i], kf.x, s0);
+        s1 = fmaf(q[4 * i + 1], kf.y, s1);
+        s0 = fmaf(q[4 * i + 2], kf.z, s0);
+        s1 = fmaf(q[4 * i + 3], kf.w, s1);
       }
+      float s = s0 + s1;
 #pragma unroll
       for (int off = Cfg::kTPQ / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
       if (c0 + kk >= limit) continue;  // masked key (uniform across the query's threads)
-      if (s > m) {
+      if (s > m + kRescaleThreshold) {
         const float alpha = fast_exp2(m - s);  // 0 on the first key (m = -inf)
         m = s;
         l *= alpha;
@@ -108,24 +124,24 @@ __global__ void __launch_bounds__(128) attention_simt_kernel(const __nv_bfloat16
       }
       const float pr = fast_exp2(s - m);
       l += pr;
-      const __nv_bfloat16* vr = sv + kk * HD + d0;
+      const float* vr = sv + kk * HD;
 #pragma unroll
-      for (int i = 0; i < Cfg::kDPT; i += 2) {
-        const float2 vf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(vr + i));
-        o[i] = fmaf(pr, vf.x, o[i]);
-        o[i + 1] = fmaf(pr, vf.y, o[i + 1]);
+      for (int i = 0; i < Cfg::kDPT / 4; ++i) {
+        const float4 vf = *reinterpret_cast<const float4*>(vr + dim_of(i));
+        o[4 * i] = fmaf(pr, vf.x, o[4 * i]);
+        o[4 * i + 1] = fmaf(pr, vf.y, o[4 * i + 1]);
+        o[4 * i + 2] = fmaf(pr, vf.z, o[4 * i + 2]);
+        o[4 * i + 3] = fmaf(pr, vf.w, o[4 * i + 3]);
       }
     }
   }
   if (!live) return;
   const float inv = l > 0.f ? 1.0f / l : 0.f;
-  __nv_bfloat16* dst = p.ctx + (row_base + qi) * p.ld_ctx + h * HD + d0;
+  __nv_bfloat16* dst = p.ctx + (row_base + qi) * p.ld_ctx + h * HD;
 #pragma unroll
-  for (int i = 0; i < Cfg::kDPT; i += 8)
-    *reinterpret_cast<uint4*>(dst + i) = make_uint4(pack_bf16x2(o[i] * inv, o[i + 1] * inv),
-                                                    pack_bf16x2(o[i + 2] * inv, o[i + 3] * inv),
-                                                    pack_bf16x2(o[i + 4] * inv, o[i + 5] * inv),
-                                                    pack_bf16x2(o[i + 6] * inv, o[i + 7] * inv));
+  for (int i = 0; i < Cfg::kDPT / 4; ++i)
+    *reinterpret_cast<uint2*>(dst + dim_of(i)) =
+        make_uint2(pack_bf16x2(o[4 * i] * inv, o[4 * i + 1] * inv), pack_bf16x2(o[4 * i + 2] * inv, o[4 * i + 3] * inv));
 }
 
 template <int HD>
