@@ -100,38 +100,65 @@ __global__ void __launch_bounds__(128) attention_simt_kernel(const __nv_bfloat16
       vd[1] = make_float4(__low2float(vh[2]), __high2float(vh[2]), __low2float(vh[3]), __high2float(vh[3]));
     }
     __syncthreads();
-    for (int kk = 0; kk < n; ++kk) {
-      const float* kr = sk + kk * HD;
-      float s0 = 0.f, s1 = 0.f;
+    // Two keys per step: their dot products and V rows are independent, so one key's shared-memory
+    // loads overlap the other's FMAs (the single-key chain was bound by shared-memory latency).
+    for (int kk = 0; kk < n; kk += 2) {
+      const bool has_b = kk + 1 < n;  // uniform across the block
+      const float* kra = sk + kk * HD;
+      const float* krb = kra + HD;
+      float sa0 = 0.f, sa1 = 0.f, sb0 = 0.f, sb1 = 0.f;
 #pragma unroll
       for (int i = 0; i < Cfg::kDPT / 4; ++i) {
-        const float4 kf = *reinterpret_cast<const float4*>(kr + dim_of(i));
-        s0 = fmaf(q[4 * i], kf.x, s0);
-        s1 = fmaf(q[4 * i + 1], kf.y, s1);
-        s0 = fmaf(q[4 * i + 2], kf.z, s0);
-        s1 = fmaf(q[4 * i + 3], kf.w, s1);
+        const float4 ka = *reinterpret_cast<const float4*>(kra + dim_of(i));
+        sa0 = fmaf(q[4 * i], ka.x, sa0);
+        sa1 = fmaf(q[4 * i + 1], ka.y, sa1);
+        sa0 = fmaf(q[4 * i + 2], ka.z, sa0);
+        sa1 = fmaf(q[4 * i + 3], ka.w, sa1);
+        if (has_b) {
+          const float4 kb = *reinterpret_cast<const float4*>(krb + dim_of(i));
+          sb0 = fmaf(q[4 * i], kb.x, sb0);
+          sb1 = fmaf(q[4 * i + 1], kb.y, sb1);
+          sb0 = fmaf(q[4 * i + 2], kb.z, sb0);
+          sb1 = fmaf(q[4 * i + 3], kb.w, sb1);
+        }
       }
-      float s = s0 + s1;
+      float sa = sa0 + sa1, sb = sb0 + sb1;
 #pragma unroll
-      for (int off = Cfg::kTPQ / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-      if (c0 + kk >= limit) continue;  // masked key (uniform across the query's threads)
-      if (s > m + kRescaleThreshold) {
-        const float alpha = fast_exp2(m - s);  // 0 on the first key (m = -inf)
-        m = s;
+      for (int off = Cfg::kTPQ / 2; off > 0; off >>= 1) {
+        sa += __shfl_xor_sync(0xffffffffu, sa, off);
+        sb += __shfl_xor_sync(0xffffffffu, sb, off);
+      }
+      // Masked keys (uniform across a query's threads); the causal limit masks a suffix.
+      const bool va = c0 + kk < limit;
+      const bool vb = has_b && c0 + kk + 1 < limit;
+      if (!va) continue;
+      const float mx = vb ? fmaxf(sa, sb) : sa;
+      if (mx > m + kRescaleThreshold) {
+        const float alpha = fast_exp2(m - mx);  // 0 on the first key (m = -inf)
+        m = mx;
         l *= alpha;
 #pragma unroll
         for (int i = 0; i < Cfg::kDPT; ++i) o[i] *= alpha;
       }
-      const float pr = fast_exp2(s - m);
-      l += pr;
-      const float* vr = sv + kk * HD;
+      const float pa = fast_exp2(sa - m);
+      const float pb = vb ? fast_exp2(sb - m) : 0.f;
+      l += pa + pb;
+      const float* vra = sv + kk * HD;
+      const float* vrb = vra + HD;
 #pragma unroll
       for (int i = 0; i < Cfg::kDPT / 4; ++i) {
-        const float4 vf = *reinterpret_cast<const float4*>(vr + dim_of(i));
-        o[4 * i] = fmaf(pr, vf.x, o[4 * i]);
-        o[4 * i + 1] = fmaf(pr, vf.y, o[4 * i + 1]);
-        o[4 * i + 2] = fmaf(pr, vf.z, o[4 * i + 2]);
-        o[4 * i + 3] = fmaf(pr, vf.w, o[4 * i + 3]);
+        const float4 va4 = *reinterpret_cast<const float4*>(vra + dim_of(i));
+        o[4 * i] = fmaf(pa, va4.x, o[4 * i]);
+        o[4 * i + 1] = fmaf(pa, va4.y, o[4 * i + 1]);
+        o[4 * i + 2] = fmaf(pa, va4.z, o[4 * i + 2]);
+        o[4 * i + 3] = fmaf(pa, va4.w, o[4 * i + 3]);
+        if (vb) {
+          const float4 vb4 = *reinterpret_cast<const float4*>(vrb + dim_of(i));
+          o[4 * i] = fmaf(pb, vb4.x, o[4 * i]);
+          o[4 * i + 1] = fmaf(pb, vb4.y, o[4 * i + 1]);
+          o[4 * i + 2] = fmaf(pb, vb4.z, o[4 * i + 2]);
+          o[4 * i + 3] = fmaf(pb, vb4.w, o[4 * i + 3]);
+        }
       }
     }
   }
