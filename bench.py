@@ -4,7 +4,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2] [--impl ours|reference]
 
 A step is one forward pass of UserOptimizedTransformer over one batch of synthetic inputs with
-the BASELINE configuration's shapes (x ~ N(0,1) and padding lengths from the reference's
+the benchmark configuration's shapes (x ~ N(0,1) and padding lengths from the reference's
 generator, weights from the reference's default init under torch.manual_seed(0)).
 
 Workloads (per GPU; multi-GPU runs are weak-scaled batch shards with no collective in the data

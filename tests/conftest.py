@@ -11,7 +11,7 @@ if str(ROOT) not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) GPU; run with -m gpu")
-    config.addinivalue_line("markers", "slow: long-running GPU parity case at a full BASELINE size")
+    config.addinivalue_line("markers", "slow: long-running GPU parity case at a full benchmark size")
 
 
 @pytest.fixture(scope="session")

@@ -31,7 +31,7 @@ HERE = Path(__file__).resolve().parent
 
 # (name, batch, seq_len, d_model, heads, ffn_dim, layers, causal, padding_ratio, seed)
 CASES = [
-    # BASELINE config 1 (the reference's CPU-runnable case).
+    # Benchmark config 1 (the reference's CPU-runnable case).
     ("c1_causal", 2, 128, 256, 4, 1024, 2, True, 0.0, 0),
     # Padding mask, non-causal, ragged lengths, S not a multiple of 128.
     ("pad_noncausal", 3, 96, 128, 2, 256, 2, False, 0.5, 1),

@@ -1,6 +1,6 @@
 """Whole-model parity on a B200: UserOptimizedTransformer (all kernels through the C-ABI) against
 the fp32 oracle on the same bf16 weights and inputs, gated by max|y - r| <= 2^-7 * max|r| with
-no NaN/Inf, plus size-independent properties at the full BASELINE sizes."""
+no NaN/Inf, plus size-independent properties at the full benchmark sizes."""
 
 import json
 from pathlib import Path
@@ -86,7 +86,7 @@ def test_model_matches_oracle_on_baseline_configs(key, batch, seq_len):
 @pytest.mark.slow
 @pytest.mark.parametrize("key,batch", [("c4", None), ("c5", 2)])
 def test_model_full_length_against_oracle(key, batch):
-    """Full BASELINE sequence length (C4: S=32768, C5: S=100000), checked against the oracle run in
+    """Full benchmark sequence length (C4: S=32768, C5: S=100000), checked against the oracle run in
     fp32 on the GPU (TF32 off)."""
     cfg, pad = _baseline_case(key, batch)
     state = oracle.round_state_to_bf16(oracle.build_reference_state(cfg, 0))

@@ -1,4 +1,4 @@
-"""Benchmark case record and the BASELINE configurations of this build.
+"""Benchmark case record and the benchmark configurations (c1-c5) this build is measured on.
 
 `TransformerConfig` mirrors the reference's frozen dataclass (transformer_benchmark/cases.py:11-38):
 same field names and order, same validation messages, so a reference TransformerConfig and this

@@ -5,7 +5,7 @@ Mirrors transformer_benchmark/runner.py: `official_case_result` (:423-441),
 `environment_metadata` (:210-220) and the timing block of `benchmark_models`
 (transformer_benchmark/timing.py:101-195), so that tools reading the reference's result files
 (e.g. its `benchmarkctl` validators) read this build's files too. Added keys are additive only:
-`"gate"` (the BASELINE tolerance, max|y - r| <= 2^-7 max|r|) next to `"accuracy"`, and per-case
+`"gate"` (the acceptance tolerance, max|y - r| <= 2^-7 max|r|) next to `"accuracy"`, and per-case
 `"implementation"` naming what produced the numbers.
 """
 
