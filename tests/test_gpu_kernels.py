@@ -391,3 +391,53 @@ def test_gemm_residual_layernorm_is_row_invariant_and_deterministic():
         outs.append((r, y))
     assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
     assert torch.equal(outs[0][0][:384], outs[2][0]) and torch.equal(outs[0][1][:384], outs[2][1])
+
+
+# ---------------------------------------------------------------------------------- cross-GPU epilogues, one GPU
+# The tensor/context-parallel entry points take every rank's buffer address; here every "rank's"
+# buffer is a local tensor, so the owner split, the extra stores and the masks run on one GPU.
+@pytest.mark.parametrize("zero", [False, True])
+def test_linear_rs_adds_rows_into_their_owner(zero):
+    m, n, k, rpr = 1000, 768, 512, 512
+    a, w, bias, ref = _gemm_inputs(m, n, k, 21)
+    g = _gen(22)
+    r0 = torch.randn(m, n, device="cuda", generator=g)
+    r1 = torch.randn(m, n, device="cuda", generator=g)
+    mask = (torch.rand(m, device="cuda", generator=g) > 0.25).to(torch.uint8)
+    res0, res1 = r0.clone(), r1.clone()
+    _capi.linear_rs(a, w, bias, zero, [res0.data_ptr(), res1.data_ptr()], 0, rpr, n, row_mask=mask)
+    keep = mask.bool()[:, None]
+    exp0, exp1 = r0.clone(), r1.clone()
+    exp0[:rpr] = torch.where(keep[:rpr], r0[:rpr] + ref[:rpr], torch.zeros_like(r0[:rpr]) if zero else r0[:rpr])
+    exp1[rpr:] = torch.where(keep[rpr:], r1[rpr:] + ref[rpr:], r1[rpr:])  # rank 1 zeroes its own masked rows
+    torch.testing.assert_close(res0, exp0, atol=2e-3, rtol=1e-4)
+    torch.testing.assert_close(res1, exp1, atol=2e-3, rtol=1e-4)
+
+
+def test_linear_bcast_stores_kv_columns_into_every_copy():
+    m, n, k, col_begin = 700, 768, 256, 256
+    a, w, bias, _ = _gemm_inputs(m, n, k, 23)
+    out0 = torch.zeros(m, n, device="cuda", dtype=torch.bfloat16)
+    out1 = torch.full((m, n), 7.0, device="cuda", dtype=torch.bfloat16)
+    _capi.linear_bcast(a, w, bias, [out0.data_ptr(), out1.data_ptr()], 0, col_begin, n)
+    plain = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    _capi.linear(a, w, bias, _capi.EPI_BIAS, plain)
+    assert torch.equal(out0, plain)
+    assert torch.equal(out1[:, col_begin:], plain[:, col_begin:])
+    assert torch.all(out1[:, :col_begin] == 7.0)
+
+
+def test_layernorm_gather_writes_every_copy():
+    rows, d = 333, 768
+    g = _gen(24)
+    x = torch.randn(rows, d, device="cuda", generator=g) * 2 + 0.3
+    w = (torch.randn(d, device="cuda", generator=g) * 0.2 + 1).bfloat16()
+    b = (torch.randn(d, device="cuda", generator=g) * 0.1).bfloat16()
+    mask = (torch.rand(rows, device="cuda", generator=g) > 0.3).to(torch.uint8)
+    y0 = torch.zeros(rows, d, device="cuda", dtype=torch.bfloat16)
+    y1 = torch.full((rows, d), 7.0, device="cuda", dtype=torch.bfloat16)
+    _capi.layernorm_gather(x, w, b, 1e-5, [y0.data_ptr(), y1.data_ptr()], row_mask=mask)
+    expect = F.layer_norm(x, (d,), w.float(), b.float(), 1e-5)
+    expect = torch.where(mask.bool()[:, None], expect, torch.zeros_like(expect))
+    assert torch.equal(y0, y1)
+    torch.testing.assert_close(y0.float(), expect, atol=1e-2, rtol=8e-3)
