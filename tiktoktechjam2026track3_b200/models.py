@@ -75,9 +75,13 @@ class _PackedBlock:
                  "w_1", "b_1", "w_2", "b_2")
 
 
-def _param_key(t: torch.Tensor) -> Tuple[int, int, torch.device, torch.dtype]:
+def _param_key(t: torch.Tensor) -> Tuple[int, int]:
+    # A move or dtype change gives new storage (data_ptr); an in-place update bumps _version.
     # Inference tensors (a model built under torch.inference_mode) carry no version counter.
-    return (t.data_ptr(), 0 if t.is_inference() else t._version, t.device, t.dtype)
+    try:
+        return (t.data_ptr(), t._version)
+    except RuntimeError:
+        return (t.data_ptr(), 0)
 
 
 class MaskLengths:
@@ -180,7 +184,26 @@ class UserOptimizedTransformer(nn.Module):
 
     # ------------------------------------------------------------------ weights
     def _weights_key(self) -> tuple:
-        return tuple(_param_key(p) for p in self.parameters())
+        """Storage address and version of every parameter, read through the fixed module structure
+        (the modules' own dicts): the generic parameters() walk cost ~280 us of host time per
+        forward at 12 layers, time during which the GPU sits idle before the first launch."""
+        key = []
+        try:
+            for layer in self.layers:
+                lm = layer._modules
+                am = lm["attention"]._modules
+                for mod in (lm["norm1"], am["q_proj"], am["k_proj"], am["v_proj"], am["out_proj"], lm["norm2"],
+                            lm["ffn_in"], lm["ffn_out"]):
+                    ps = mod._parameters
+                    w, b = ps["weight"], ps["bias"]
+                    key.append((w.data_ptr(), w._version))
+                    key.append((b.data_ptr(), b._version))
+            fp = self.final_norm._parameters
+            key.append((fp["weight"].data_ptr(), fp["weight"]._version))
+            key.append((fp["bias"].data_ptr(), fp["bias"]._version))
+        except RuntimeError:  # inference tensors have no version counter
+            return tuple(_param_key(p) for p in self.parameters())
+        return tuple(key)
 
     def packed_weights(self) -> List[_PackedBlock]:
         """Per-block bf16 weights, with q/k/v packed into one [3D, D] projection (cached).
