@@ -208,3 +208,26 @@ def test_layernorm_fused_and_separate_agree(key, batch, seq_len):
     assert baseline_gate(outs[True], outs[False].float()).passed
     if pad > 0:
         assert torch.all(outs[True][~mask] == 0)
+
+
+def test_in_place_qkv_update_is_seen_on_the_next_call():
+    """forward() launches with the weights packed on the previous call and checks for parameter
+    changes afterwards; an in-place change of a weight that lives only in a packed copy (k_proj in
+    the packed QKV projection) must still show in that call's output, graph replay or eager."""
+    cfg = TransformerConfig(2, 256, 256, 4, 512, 2, True)
+    model = _model(cfg, oracle.build_reference_state(cfg, 0))
+    x = torch.randn(2, 256, 256, device="cuda").bfloat16()
+    with torch.inference_mode():
+        a = model(x)
+    with torch.no_grad():
+        model.layers[1].attention.k_proj.weight.mul_(0.5)
+    with torch.inference_mode():
+        b = model(x)
+        model.use_cuda_graph = False
+        b_eager = model(x)
+        fresh = UserOptimizedTransformer(cfg)
+        fresh.load_state_dict({k: v.detach().clone() for k, v in model.state_dict().items()}, strict=True)
+        fresh = fresh.to(device="cuda", dtype=torch.bfloat16).eval()
+        c = fresh(x)
+    assert not torch.equal(a, b)
+    assert torch.equal(b, b_eager) and torch.equal(b, c)
