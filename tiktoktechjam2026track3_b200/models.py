@@ -414,6 +414,7 @@ class _GraphedStack:
         self.model = model
         self.packed = packed
         self.ws = _Workspace(model.config, batch, seq_len, device)
+        self._src = (None, None)  # the mask tensors last copied into kv_len / row_mask
         self.kv_len = torch.zeros(batch, device=device, dtype=torch.int32) if masked else None
         self.row_mask = torch.zeros(batch * seq_len, device=device, dtype=torch.uint8) if masked else None
         self.ws.resid.zero_()
@@ -429,9 +430,12 @@ class _GraphedStack:
             model._blocks(self.ws, batch, seq_len, self.kv_len, self.row_mask, packed, fused)
 
     def run(self, x2: torch.Tensor, kv_len, row_mask, out2: torch.Tensor) -> None:
-        if self.kv_len is not None:
+        if self.kv_len is not None and (kv_len is not self._src[0] or row_mask is not self._src[1]):
+            # The mask cache hands back the same tensors only for an unchanged mask (same storage
+            # and version), so their copies are already in the static buffers.
             self.kv_len.copy_(kv_len)
             self.row_mask.copy_(row_mask)
+            self._src = (kv_len, row_mask)
         pb0 = self.packed[0]
         _capi.layernorm(x2, pb0.ln1_w, pb0.ln1_b, pb0.ln1_eps, self.ws.ln, resid_out=self.ws.resid)
         self.graph.replay()
