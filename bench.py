@@ -5,27 +5,32 @@
 
 A step is one forward pass of UserOptimizedTransformer over one batch of synthetic inputs with
 the benchmark configuration's shapes (x ~ N(0,1) and padding lengths from the reference's
-generator, weights from the reference's default init under torch.manual_seed(0)).
+generator with seed 100000, weights from the reference's default init under torch.manual_seed(0)).
 
-Workloads (per GPU; multi-GPU runs are weak-scaled batch shards with no collective in the data
-path, one process per GPU launched by torch.distributed.run):
+Workloads (the benchmark configurations; the global batch is fixed, so N GPUs split the same
+work — strong scaling — one process per GPU launched by torch.distributed.run):
   c2 (default)  B=8  S=512    D=768  H=12 F=3072 L=12, padding mask (lengths in [256, 512])
   c3            B=16 S=2048   D=1024 H=16 F=4096 L=4, causal
-  c5            B=4  S=100000 D=1024 H=16 F=1024 L=2, causal (x8 GPUs = the B=32 configuration)
+  c5            B=32 S=100000 D=1024 H=16 F=1024 L=2, causal (4 sequences per GPU on 8 GPUs)
   c1            B=2  S=128    D=256  H=4  F=1024 L=2, causal
-  c4            B=1  S=32768  D=2048 H=16 F=8192 L=2, causal (single GPU)
+  c4            B=1  S=32768  D=2048 H=16 F=8192 L=2, causal
+With B >= N every rank runs a contiguous shard of B/N sequences (no collective in the data path);
+with B < N the sequence is split over the ranks (context parallel by default, tensor parallel with
+--split tp). --per-gpu-batch B' runs B' sequences on every rank instead (weak scaling).
 
-Reported (rank 0): `value` = tokens/s of the whole job with inputs resident in HBM, each of the K
-timed steps bracketed by barrier + synchronize and timed with CUDA events on the launching
-stream, L2 flushed (256 MiB write) before every step, max over ranks; `e2e` = the same forward
-through the public module API with the step's input copied from pinned host memory and the
-output copied back inside the timed region; `roofline` = the dominant kernel (by device time)
-against the measured bf16 tensor peak; `cpu_baseline` = the fp32 CPU restatement of the
-reference (oracle/) on a bounded sample, on the host's cores.
+Reported (rank 0): `value` = tokens/s of the whole job (B*S of the global batch per step) with
+inputs resident in HBM, each of the K timed steps bracketed by barrier + synchronize and timed
+with CUDA events on the launching stream, L2 flushed (256 MiB write) before every step, max over
+ranks; `e2e` = the same forward through the public module API with each rank's input copied from
+pinned host memory and the output copied back inside the timed region; `roofline` = the dominant
+kernel class (by device time) against the measured peak, with its time both as launched alone
+(per-launch CUDA events) and as its share of the measured step; `cpu_baseline` = the fp32 CPU
+restatement of the reference (oracle/) on a bounded sample, on the host's cores.
 
-`--impl reference` times the reference computation on the host CPU instead (fp32, all host
-threads, the oracle port of BaselineTransformer.forward) and prints the same line with
-"impl": "reference"; under torch.distributed.run only rank 0 runs it.
+`--impl reference` times the same CPU sample as the reference arm (fp32, all host threads, the
+oracle port of BaselineTransformer.forward; median of the K steps, the statistic cpu_baseline
+uses) and prints the same line with "impl": "reference"; under torch.distributed.run only rank 0
+runs it.
 """
 
 from __future__ import annotations
@@ -51,14 +56,22 @@ from tiktoktechjam2026track3_b200.cases import BASELINE_CONFIGS, TransformerConf
 
 METRIC = "forward_tokens_per_sec"
 UNIT = "tokens/s"
-PER_GPU_BATCH = {"c1": 2, "c2": 8, "c3": 16, "c4": 1, "c5": 4}
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 L2_FLUSH_BYTES = 256 << 20
 LONG_STEP_MS = 50.0
-# DRAM bytes (read + write) per launch of the dominant kernel class, averaged over the class's
-# launches in one forward, from an ncu capture of this bench (profiles/launches_bench_c2.md):
-# key = (workload, tensor-parallel ranks, kernel class, LayerNorm fused into the residual GEMMs).
-DRAM_BYTES_PER_LAUNCH = {("c2", 1, "gemm_tc_kernel", False): 19224147.2}
+TRAFFIC_FILE = ROOT / "tiktoktechjam2026track3_b200" / "data" / "ncu_dram_traffic.json"
+
+
+def dram_traffic(workload: str, world: int, kernel: str, ln_fused: bool):
+    """DRAM bytes per launch of `kernel` from the committed ncu figures (None if not captured)."""
+    try:
+        entries = json.loads(TRAFFIC_FILE.read_text())["entries"]
+    except (OSError, ValueError, KeyError):
+        return None, None
+    for e in entries:
+        if (e["workload"], e["world"], e["kernel"], e["layernorm_fused"]) == (workload, world, kernel, ln_fused):
+            return e["bytes_per_launch"], e["source"]
+    return None, None
 
 
 def parse_args(argv=None):
@@ -76,15 +89,19 @@ def parse_args(argv=None):
     p.add_argument("--fuse-ln", default="auto", choices=("auto", "on", "off"),
                    help="LayerNorm inside the out_proj / ffn_out GEMM epilogues (auto: where the library recommends "
                         "it; nowhere in this build, it measured slower than the separate LayerNorm)")
+    p.add_argument("--per-gpu-batch", type=int, default=0,
+                   help="sequences per GPU (weak scaling); default 0 = split the configuration's global batch")
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
     p.add_argument("--cpu-seconds", type=float, default=15.0, help="target CPU time of the CPU baseline sample")
     return p.parse_args(argv)
 
 
-def workload_config(name: str) -> tuple[TransformerConfig, float]:
+def workload_config(name: str, batch: int = 0) -> tuple[TransformerConfig, float]:
+    """The benchmark configuration `name` (its global batch, or `batch` sequences if given)."""
     w = BASELINE_CONFIGS[name]
     c = w.config
-    cfg = TransformerConfig(PER_GPU_BATCH[name], c.seq_len, c.d_model, c.num_heads, c.ffn_dim, c.num_layers, c.causal)
+    cfg = TransformerConfig(batch or c.batch_size, c.seq_len, c.d_model, c.num_heads, c.ffn_dim, c.num_layers,
+                            c.causal)
     return cfg, w.padding_ratio
 
 
@@ -214,12 +231,15 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- CPU legs (oracle)
-def cpu_reference_sample(cfg: TransformerConfig, padding_ratio: float, threads: int):
-    """One sequence of the workload through the fp32 CPU restatement of the reference."""
+def cpu_sample(cfg: TransformerConfig, padding_ratio: float, threads: int):
+    """The bounded CPU sample of a workload: one sequence through the fp32 CPU restatement of the
+    reference (all layers; for S = 100000 one of the layers, the time then scaled by the layer
+    count — every layer does the same work). Returns (step, tokens per step, layer scale, text)."""
     from oracle import reference_fp32 as oracle  # CPU baseline / reference arm only
 
     torch.set_num_threads(threads)
-    sample_cfg = TransformerConfig(1, cfg.seq_len, cfg.d_model, cfg.num_heads, cfg.ffn_dim, cfg.num_layers, cfg.causal)
+    layers = 1 if cfg.seq_len >= 65536 else cfg.num_layers
+    sample_cfg = TransformerConfig(1, cfg.seq_len, cfg.d_model, cfg.num_heads, cfg.ffn_dim, layers, cfg.causal)
     state = oracle.build_reference_state(sample_cfg, 0)
     x, mask = oracle.generate_random_case(sample_cfg, torch.device("cpu"), torch.float32, 100000, padding_ratio)
     use_mask = None if padding_ratio <= 0 else mask
@@ -228,31 +248,63 @@ def cpu_reference_sample(cfg: TransformerConfig, padding_ratio: float, threads: 
         with torch.inference_mode():
             oracle.forward(state, sample_cfg, x, use_mask, query_chunk=2048)
 
-    return sample_cfg, step
+    text = (f"1 sequence (S={cfg.seq_len}, {layers} of {cfg.num_layers} layers) of the workload through the fp32 CPU "
+            f"restatement of BaselineTransformer.forward (oracle/reference_fp32.py, attention in 2048-query chunks), "
+            f"{threads} threads")
+    return step, cfg.seq_len, cfg.num_layers / layers, text
+
+
+def reference_path_record(cfg: TransformerConfig):
+    """Whether the reference's own path (BaselineSelfAttention materialises [B, H, S, S] scores,
+    models.py:55-75) fits this host for one sequence; None when it does. The reference's runner
+    records a run that dies of memory as execution_failed / out_of_memory (runner.py:445-460,
+    527-531); here the need is computed instead of provoked on a shared host."""
+    try:
+        import psutil
+
+        host = psutil.virtual_memory().total
+    except Exception:  # noqa: BLE001 - psutil missing: no prediction
+        return None
+    scores = cfg.num_heads * float(cfg.seq_len) ** 2 * 4  # one fp32 [1, H, S, S] copy
+    need = 4 * scores  # scores, scaled/masked copy, softmax output and its bf16/fp32 round trip
+    if need <= 0.8 * host:
+        return None
+    return {"status": "execution_failed", "failure_category": "out_of_memory",
+            "error": (f"not run (predicted): one sequence needs ~4 fp32 [1, {cfg.num_heads}, {cfg.seq_len}, "
+                      f"{cfg.seq_len}] score copies = {need / 1e9:.0f} GB against {host / 1e9:.0f} GB of host memory")}
+
+
+def cpu_times(step, target_seconds: float, max_samples: int, min_samples: int = 1):
+    """Runs `step` until target_seconds have passed (at least min_samples, at most max_samples),
+    after one warm-up unless a single step is longer than a quarter of the target."""
+    t0 = time.perf_counter()
+    step()
+    first = time.perf_counter() - t0
+    times = [] if first < target_seconds / 4 else [first]
+    t_begin = time.perf_counter()
+    while len(times) < max_samples and (len(times) < min_samples or time.perf_counter() - t_begin < target_seconds):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    return times
 
 
 def run_cpu_baseline(cfg, padding_ratio, target_seconds: float) -> dict:
     threads = os.cpu_count() or 1
-    sample_cfg, step = cpu_reference_sample(cfg, padding_ratio, threads)
-    step()  # warm-up
-    times = []
-    t_begin = time.perf_counter()
-    while True:
-        t0 = time.perf_counter()
-        step()
-        times.append(time.perf_counter() - t0)
-        if time.perf_counter() - t_begin > target_seconds or len(times) >= 50:
-            break
-    per = statistics.median(times)
-    tokens = sample_cfg.batch_size * sample_cfg.seq_len
-    return {
+    step, tokens, layer_scale, text = cpu_sample(cfg, padding_ratio, threads)
+    times = cpu_times(step, target_seconds, max_samples=50)
+    per = statistics.median(times) * layer_scale
+    rec = {
         "value": tokens / per,
         "unit": UNIT,
         "cores": threads,
         "kind": "port",
-        "sample": f"{len(times)} forwards of 1 sequence (S={cfg.seq_len}, L={cfg.num_layers}) in fp32 on CPU "
-                  f"(oracle restatement of BaselineTransformer.forward), median {per * 1e3:.1f} ms",
+        "sample": f"median of {len(times)} forwards of {text}: {per * 1e3:.1f} ms per sequence",
     }
+    ref_path = reference_path_record(cfg)
+    if ref_path is not None:
+        rec["reference_path"] = ref_path
+    return rec
 
 
 def run_reference_arm(args) -> None:
@@ -261,7 +313,7 @@ def run_reference_arm(args) -> None:
         return
     cfg, pad = workload_config(args.workload)
     threads = os.cpu_count() or 1
-    sample_cfg, step = cpu_reference_sample(cfg, pad, threads)
+    step, tokens, layer_scale, text = cpu_sample(cfg, pad, threads)
     for _ in range(max(args.warmup, 0)):
         step()
     times = []
@@ -269,11 +321,13 @@ def run_reference_arm(args) -> None:
         t0 = time.perf_counter()
         step()
         times.append(time.perf_counter() - t0)
-    per = sum(times) / len(times)
-    tokens = sample_cfg.batch_size * sample_cfg.seq_len
+    per = statistics.median(times) * layer_scale
     value = tokens / per
-    sample = (f"each step: 1 sequence (S={cfg.seq_len}) of the workload through the fp32 CPU restatement of "
-              f"BaselineTransformer.forward (oracle/reference_fp32.py), {threads} threads")
+    sample = f"each step: {text}; median of the {args.steps} steps"
+    cpu = {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
+    ref_path = reference_path_record(cfg)
+    if ref_path is not None:
+        cpu["reference_path"] = ref_path
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -284,20 +338,30 @@ def run_reference_arm(args) -> None:
         "warmup": args.warmup,
         "ms_per_step": per * 1e3,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": args.workload, "model": "transformer_encoder", "global_batch": 1,
+        "config": {"workload": args.workload, "model": "transformer_encoder", "global_batch": cfg.batch_size,
                    "seq_len": cfg.seq_len, "d_model": cfg.d_model, "layers": cfg.num_layers,
-                   "parallelism": "cpu", "sample_of_per_gpu_batch": cfg.batch_size},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+                   "parallelism": "cpu", "sample_sequences_per_step": 1},
+        "cpu_baseline": cpu,
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
 # ----------------------------------------------------------------------------- GPU arm
+def class_times(log, reps: int):
+    """Per launch kind: device ms per forward and launches per forward, from a launch log."""
+    kind_ms: dict = {}
+    kind_n: dict = {}
+    for kind, s, e in log:
+        kind_ms[kind] = kind_ms.get(kind, 0.0) + s.elapsed_time(e) / reps
+        kind_n[kind] = kind_n.get(kind, 0) + 1
+    return kind_ms, {k: v // reps for k, v in kind_n.items()}
+
+
 def main() -> None:
     args = parse_args()
     if args.impl == "reference":
@@ -320,35 +384,53 @@ def main() -> None:
         os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep stdout to the one JSON line
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
 
-    cfg, pad = workload_config(args.workload)
+    weak = args.per_gpu_batch > 0
+    gcfg, pad = workload_config(args.workload, args.per_gpu_batch * world if weak else 0)
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.manual_seed(0)
-    # A batch smaller than the GPU count (c4: one sequence) is split over all ranks — context
-    # parallel by default, tensor parallel with --split tp — (strong scaling); everything else
-    # gives each rank its own batch shard (weak scaling).
-    tensor_parallel = world > 1 and cfg.batch_size < world
-    if tensor_parallel:
+    # The global batch is split over the ranks: B >= N gives every rank a contiguous shard of
+    # whole sequences (no collective in the data path); B < N splits each sequence over the ranks
+    # (context parallel by default, tensor parallel with --split tp).
+    split_sequences = world > 1 and gcfg.batch_size < world
+    x_all, mask_all = generate_random_case(gcfg, device, torch.bfloat16, 100000, pad)
+    if split_sequences:
         from tiktoktechjam2026track3_b200.sharding import ContextParallelTransformer, TensorParallelTransformer
 
+        cfg = gcfg
         full = UserOptimizedTransformer(cfg)
         if args.split == "cp":
             model = ContextParallelTransformer(cfg, full.state_dict(), device)
         else:
             model = TensorParallelTransformer(cfg, full.state_dict(), device, collective=args.collective)
         del full
-        x, mask = generate_random_case(cfg, device, torch.bfloat16, 100000, pad)
+        x, mask = x_all, mask_all
+        shard = (0, gcfg.batch_size)
     else:
+        from tiktoktechjam2026track3_b200.sharding import batch_shard
+
+        shard = batch_shard(gcfg.batch_size, world, rank)
+        cfg = TransformerConfig(shard[1] - shard[0], gcfg.seq_len, gcfg.d_model, gcfg.num_heads, gcfg.ffn_dim,
+                                gcfg.num_layers, gcfg.causal)
         model = UserOptimizedTransformer(cfg).to(device=device, dtype=torch.bfloat16).eval()
         model.fuse_layernorm = {"auto": "auto", "on": True, "off": False}[args.fuse_ln]
-        x, mask = generate_random_case(cfg, device, torch.bfloat16, 100000 + rank, pad)
-    ln_fused = (not tensor_parallel) and model.layernorm_fused(cfg.batch_size * cfg.seq_len)
+        x = x_all[shard[0]:shard[1]].contiguous()
+        mask = mask_all[shard[0]:shard[1]].contiguous()
+    del x_all, mask_all
+    ln_fused = (not split_sequences) and model.layernorm_fused(cfg.batch_size * cfg.seq_len)
     lengths = mask.sum(1).tolist() if pad > 0 else None
-    use_mask = mask if pad > 0 else mask  # the harness always passes a mask; all-true masks are elided
+    use_mask = mask  # the harness always passes a mask; all-true masks are elided by the model
     flush = torch.empty(L2_FLUSH_BYTES // 4, device=device, dtype=torch.float32)
 
     def barrier():
         if dist is not None:
             dist.barrier()
+
+    def gather(obj):
+        if dist is None:
+            return [obj]
+        out = [None] * world
+        dist.all_gather_object(out, obj)
+        return out
 
     with torch.inference_mode():
         for _ in range(args.warmup):
@@ -377,7 +459,7 @@ def main() -> None:
             dist.all_reduce(total_ms, op=dist.ReduceOp.MAX)
         total_ms = float(total_ms.item())
         ms_per_step = total_ms / args.steps
-        tokens_per_step = cfg.batch_size * cfg.seq_len * (1 if tensor_parallel else world)
+        tokens_per_step = gcfg.batch_size * gcfg.seq_len
         value = tokens_per_step / (ms_per_step / 1e3)
 
         # ---------------- end to end through the public API, host buffers
@@ -406,10 +488,15 @@ def main() -> None:
         e2e_per_step = float(e2e_total.item()) / args.steps
         h2d = x_host.numel() * x_host.element_size() + m_host.numel() * m_host.element_size()
         d2h = y_host.numel() * y_host.element_size()
+        # Every rank copies its own shard (sequence-split plans: the whole, replicated, input).
+        io_bytes = gather((h2d, d2h))
 
         # ---------------- per-kernel device times (roofline of the dominant kernel)
         # Each eager forward is queued behind a ~20 ms GPU sleep, so the host enqueues every launch
         # before the GPU reaches it and the per-launch events time the kernels, not launch overhead.
+        # Events between launches break the programmatic-dependent-launch overlap of the graph
+        # replayed in the timed steps, so these are launch-alone times; each class is also
+        # reported as its share of the measured step.
         model.record_launches(True)
         reps = 3
         for _ in range(reps):
@@ -419,17 +506,17 @@ def main() -> None:
         torch.cuda.synchronize()
         log = model.take_launch_log()
         model.record_launches(False)
+        model._status.check(wait=True)  # a timed-out kernel invalidates the run
 
-    kind_ms: dict = {}
-    kind_n: dict = {}
-    for kind, s, e in log:
-        kind_ms[kind] = kind_ms.get(kind, 0.0) + s.elapsed_time(e) / reps
-        kind_n[kind] = kind_n.get(kind, 0) + 1
+    kind_ms, kind_n = class_times(log, reps)
+    per_rank = gather({"rank": rank, "ms_per_step": sum(step_ms) / args.steps,
+                       "sequences": shard[1] - shard[0] if not split_sequences else gcfg.batch_size,
+                       "tokens_valid": int(sum(lengths)) if lengths is not None else cfg.batch_size * cfg.seq_len,
+                       "ms_by_launch_kind": {k: round(v, 4) for k, v in sorted(kind_ms.items())}})
     flops = gemm_flops(cfg)
     attn = attention_flops(cfg, lengths)
-    gemm_ms = sum(v for k, v in kind_ms.items() if k.startswith("gemm"))
     gemm_total = sum(flops.values())
-    if tensor_parallel:  # per-rank work: heads and FFN columns are split over the ranks
+    if split_sequences:  # per-rank work: heads / FFN columns or token rows are split over the ranks
         gemm_total /= world
         attn /= world
     peaks, peak_src = measured_peaks()
@@ -439,29 +526,36 @@ def main() -> None:
     tensor_peak = peaks["bf16_tflops_sustained"] if long_step else peaks["bf16_tflops"]
     tensor_peak_name = "bf16 sustained" if long_step else "bf16 burst"
     classes = {
-        "gemm_tc_kernel": {"ms": gemm_ms, "work": gemm_total, "bound": "tensor",
-                           "launches": sum(v for k, v in kind_n.items() if k.startswith("gemm")) // reps},
+        "gemm_tc_kernel": {"ms": sum(v for k, v in kind_ms.items() if k.startswith("gemm")), "work": gemm_total,
+                           "bound": "tensor",
+                           "launches": sum(v for k, v in kind_n.items() if k.startswith("gemm"))},
         "attention_pair_kernel": {"ms": kind_ms.get("attention", 0.0), "work": attn, "bound": "tensor",
-                                "launches": kind_n.get("attention", 0) // reps},
-        "layernorm_vec_kernel": {"ms": kind_ms.get("layernorm", 0.0), "work": layernorm_bytes(cfg, ln_fused), "bound": "hbm",
-                                 "launches": kind_n.get("layernorm", 0) // reps},
+                                  "launches": kind_n.get("attention", 0)},
+        "layernorm_vec_kernel": {"ms": kind_ms.get("layernorm", 0.0), "work": layernorm_bytes(cfg, ln_fused),
+                                 "bound": "hbm", "launches": kind_n.get("layernorm", 0)},
     }
+    if split_sequences:
+        classes["layernorm_vec_kernel"]["work"] /= world
+    # This rank's step time spread over its launch kinds in proportion to their launch-alone times.
+    my_step = sum(step_ms) / args.steps
+    alone_sum = sum(kind_ms.values())
+    in_step_scale = my_step / alone_sum if alone_sum > 0 else 0.0
     kernels = {}
     for name, c in classes.items():
         if c["ms"] <= 0:
             continue
-        if c["bound"] == "tensor":
-            achieved = c["work"] / (c["ms"] / 1e3) / 1e12
-            peak = tensor_peak
-            unit = "TFLOP/s"
-        else:
-            achieved = c["work"] / (c["ms"] / 1e3) / 1e9
-            peak = peaks["hbm_gbs"]
-            unit = "GB/s"
+        peak = tensor_peak if c["bound"] == "tensor" else peaks["hbm_gbs"]
+        div = 1e12 if c["bound"] == "tensor" else 1e9
+        achieved = c["work"] / (c["ms"] / 1e3) / div
+        in_step_ms = c["ms"] * in_step_scale
+        achieved_in_step = c["work"] / (in_step_ms / 1e3) / div
         kernels[name] = {"ms_per_step": c["ms"], "launches_per_step": c["launches"], "achieved": achieved,
-                         "unit": unit, "frac": achieved / peak}
+                         "unit": "TFLOP/s" if c["bound"] == "tensor" else "GB/s", "frac": achieved / peak,
+                         "in_step_ms": in_step_ms, "achieved_in_step": achieved_in_step,
+                         "frac_in_step": achieved_in_step / peak}
     dominant = max(classes, key=lambda k: classes[k]["ms"])
     dk = kernels[dominant]
+    traffic, traffic_src = dram_traffic(args.workload, world, dominant, ln_fused) if not weak else (None, None)
     roofline = {
         "kernel": dominant,
         "bound": classes[dominant]["bound"],
@@ -470,7 +564,13 @@ def main() -> None:
         "peak_source": f"{peak_src} ({tensor_peak_name if classes[dominant]['bound'] == 'tensor' else 'HBM copy'})",
         "unit": dk["unit"],
         "frac": dk["frac"],
-        "traffic": DRAM_BYTES_PER_LAUNCH.get((args.workload, world if tensor_parallel else 1, dominant, ln_fused)),
+        "achieved_in_step": dk["achieved_in_step"],
+        "frac_in_step": dk["frac_in_step"],
+        "timing": ("achieved/frac: launch-alone CUDA events around each launch of the class (eager pass); "
+                   "*_in_step: the measured step time split over the launch kinds in proportion to those times "
+                   f"(launch-alone sum {alone_sum:.4f} ms vs step {my_step:.4f} ms on rank {rank})"),
+        "traffic": traffic,
+        "traffic_source": traffic_src,
         "work_per_launch": classes[dominant]["work"] / max(1, classes[dominant]["launches"]),
     }
     total_flops = gemm_total + attn  # per rank
@@ -478,9 +578,11 @@ def main() -> None:
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = run_cpu_baseline(cfg, pad, args.cpu_seconds)
+        cpu = run_cpu_baseline(gcfg, pad, args.cpu_seconds)
 
     if rank == 0:
+        slowest = max(per_rank, key=lambda r: r["ms_per_step"])
+        slow_kinds = slowest["ms_by_launch_kind"]
         line = {
             "metric": METRIC,
             "value": value,
@@ -490,33 +592,35 @@ def main() -> None:
             "warmup": args.warmup,
             "ms_per_step": ms_per_step,
             "higher_is_better": True,
-            "scaling": "strong" if tensor_parallel else "weak",
+            "scaling": "weak" if weak else "strong",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic",
             "config": {
                 "workload": args.workload,
                 "model": "transformer_encoder",
-                "global_batch": cfg.batch_size * (1 if tensor_parallel else world),
-                "seq_len": cfg.seq_len,
-                "d_model": cfg.d_model,
-                "heads": cfg.num_heads,
-                "ffn_dim": cfg.ffn_dim,
-                "layers": cfg.num_layers,
-                "causal": cfg.causal,
+                "global_batch": gcfg.batch_size,
+                "seq_len": gcfg.seq_len,
+                "d_model": gcfg.d_model,
+                "heads": gcfg.num_heads,
+                "ffn_dim": gcfg.ffn_dim,
+                "layers": gcfg.num_layers,
+                "causal": gcfg.causal,
                 "padding_ratio": pad,
                 "parallelism": (f"cp{world} (each sequence's tokens in 2 x {world} zigzag chunks; Q/K/V rows "
                                 "all-gathered over NVLink into every GPU's full-length buffer, attention of the "
                                 "rank's query rows, LayerNorms and GEMMs on its own rows; 2 flag barriers per block)")
-                if tensor_parallel and model.collective == "cp" else
+                if split_sequences and model.collective == "cp" else
                 (f"tp{world} (heads / FFN columns; " + {
                     "rs": "out_proj / ffn_out GEMM epilogues add each row into its owner's fp32 residual over "
                           "NVLink (reduce-scatter), owners' LayerNorm rows stored into every GPU's buffer (all-gather), "
                           "4 flag barriers per block)",
                     "nccl": "2 NCCL all-reduces of the fp32 [T, D] partial per block)"}[model.collective])
-                if tensor_parallel else f"dp{world} (batch shards, no collective)",
+                if split_sequences else
+                f"dp{world} (batch shards, {'/'.join(str(r['sequences']) for r in per_rank)} sequences per GPU, "
+                "no collective)",
                 "l2": "flushed (256 MiB write) before every timed step",
-                "launches": (f"eager launches ({model.collective})" if tensor_parallel else
+                "launches": (f"eager launches ({model.collective})" if split_sequences else
                              "first/final LayerNorm eager, the block launches replayed from a CUDA graph"),
                 "layernorm": ("norm2 and the next block's norm1 in the out_proj / ffn_out GEMM epilogues "
                               "(clusters spanning each row)") if ln_fused else "separate LayerNorm launches",
@@ -524,21 +628,25 @@ def main() -> None:
             "roofline": roofline,
             "kernels": kernels,
             "model_flops_per_step": total_flops * world,
-            "allreduce_ms_per_step": kind_ms.get("allreduce", 0.0),
-            "barrier_ms_per_step": kind_ms.get("barrier", 0.0),
             "ms_per_step_by_launch_kind": {k: round(v, 4) for k, v in sorted(kind_ms.items())},
+            "per_rank": per_rank if world > 1 else None,
+            "limiter": ({"rank": slowest["rank"], "ms_per_step": slowest["ms_per_step"],
+                         "kind": max(slow_kinds, key=slow_kinds.get) if slow_kinds else None,
+                         "note": "the slowest rank sets the step; its largest launch kind (launch-alone times)"}
+                        if world > 1 else None),
             "mfu_of_bf16_peak": mfu,
             "cpu_baseline": cpu,
             "e2e": {"value": tokens_per_step / (e2e_per_step / 1e3), "unit": UNIT, "ms_per_step": e2e_per_step,
-                    "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world},
-            "gpu_launches": args.steps * (model.launches_per_forward(cfg.num_layers) if tensor_parallel else
+                    "h2d_bytes_per_step": sum(b[0] for b in io_bytes),
+                    "d2h_bytes_per_step": sum(b[1] for b in io_bytes)},
+            "gpu_launches": args.steps * (model.launches_per_forward(cfg.num_layers) if split_sequences else
                                           UserOptimizedTransformer.launches_per_forward(cfg.num_layers, ln_fused)),
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
     if dist is not None:
         torch.cuda.synchronize()
-        if tensor_parallel:
+        if split_sequences:
             model.close()
         dist.barrier()
         dist.destroy_process_group()

@@ -57,6 +57,13 @@ const char* b2_last_error(void);
  * reason, kernel 2 = linear, 3 = attention. Synchronous: it waits for the device. */
 int b2_device_status(uint32_t* out_status, int clear);
 
+/* Enqueues a copy of the current device's status word (the value b2_device_status reads, not
+ * cleared) into host_dst on `stream`, behind the work already enqueued there; host_dst should be
+ * pinned host memory, valid until the copy completes. Lets a caller check every forward pass for
+ * a pipeline timeout without synchronising: read *host_dst once an event recorded after this call
+ * has completed. No counterpart in the reference (its kernels have no bounded waits). */
+int b2_device_status_async(uint32_t* host_dst, void* stream);
+
 /*
  * LayerNorm over the last dimension: y = (x - mean) / sqrt(var + eps) * gamma + beta, fp32
  * statistics, bf16 y. Replaces nn.LayerNorm in BaselineTransformerBlock (models.py:721, 723) and

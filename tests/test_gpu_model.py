@@ -231,3 +231,55 @@ def test_in_place_qkv_update_is_seen_on_the_next_call():
         c = fresh(x)
     assert not torch.equal(a, b)
     assert torch.equal(b, b_eager) and torch.equal(b, c)
+
+
+def test_freed_mask_storage_reused_by_a_different_mask():
+    """A mask freed after a call, and a different prefix mask of the same shape allocated next
+    (the caching allocator tends to hand back the same block): the second call must use the new
+    lengths, graph replay included."""
+    cfg = TransformerConfig(2, 256, 256, 4, 512, 2, False)
+    model = _model(cfg, oracle.build_reference_state(cfg, 0))
+    x = torch.randn(2, 256, 256, device="cuda").bfloat16()
+    lengths_a = torch.tensor([[100], [256]], device="cuda")
+    lengths_b = torch.tensor([[200], [60]], device="cuda")
+    pos = torch.arange(256, device="cuda")[None, :]
+    mask = pos < lengths_a
+    with torch.inference_mode(False):
+        mask = mask.clone()  # an ordinary (versioned) tensor, as the harness's timing input is
+    with torch.inference_mode():
+        a = model(x, mask)
+    del mask
+    torch.cuda.synchronize()
+    with torch.inference_mode(False):
+        mask_b = (pos < lengths_b).clone()
+    with torch.inference_mode():
+        b = model(x, mask_b)
+        fresh = _model(cfg, {k: v.detach().clone() for k, v in model.state_dict().items()})
+        b_ref = fresh(x, mask_b)
+    assert not torch.equal(a, b)
+    assert torch.equal(b, b_ref)
+    assert torch.all(b[1, 60:] == 0) and torch.all(b[0, 200:] == 0)
+
+
+def test_forward_reports_a_kernel_timeout_of_an_earlier_call():
+    """The status word is checked on every call without a sync: after a kernel gave up waiting (a
+    peer barrier whose peer never signals, the allowed way to make a wait run out), the next
+    forward raises, and check_device_status() raises once the copy has landed."""
+    cfg = TransformerConfig(1, 128, 256, 4, 512, 1, True)
+    model = _model(cfg, oracle.build_reference_state(cfg, 0))
+    x = torch.randn(1, 128, 256, device="cuda").bfloat16()
+    with torch.inference_mode():
+        model(x)
+    model.check_device_status()  # clean
+    pads = torch.zeros(2, _capi.PAD_WORDS, dtype=torch.int32, device="cuda")
+    _capi.peer_barrier([pads[0].data_ptr(), pads[1].data_ptr()], 0, 0, pads.device)  # times out (4 s)
+    with torch.inference_mode():
+        model(x)  # enqueued behind the barrier: its status copy sees the timeout
+    with pytest.raises(RuntimeError, match="gave up waiting"):
+        model.check_device_status()
+    status = _capi.device_status(clear=True)
+    assert status >> 16 == 4 and status & 0xFF == 1, hex(status)
+    with torch.inference_mode():
+        y = model(x)  # the word was cleared and the failed copy consumed: runs again
+    model.check_device_status()
+    assert torch.isfinite(y.float()).all()

@@ -144,3 +144,49 @@ def test_layernorm_fusion_policy_depends_on_widths_only():
     assert not odd.layernorm_fused(8)
     assert UserOptimizedTransformer.launches_per_forward(12, True) == 62
     assert UserOptimizedTransformer.launches_per_forward(12) == 85
+
+
+def test_mask_cache_keeps_its_mask_alive():
+    """The cache entry holds the mask tensor, so a freed mask's storage cannot come back as a
+    different mask of the same shape that the entry would still match (same address, same version)."""
+    model = UserOptimizedTransformer(TransformerConfig(2, 8, 16, 4, 32, 1, False))
+    mask = torch.arange(8)[None, :] < torch.tensor([[3], [8]])
+    ptr = mask.data_ptr()
+    assert model.mask_to_lengths(mask, 2, 8)[0].tolist() == [3, 8]
+    del mask
+    cached = model._mask_lengths._cache
+    assert cached is not None and cached[1].data_ptr() == ptr  # still owned by the cache
+    other = torch.arange(8)[None, :] < torch.tensor([[5], [2]])
+    assert other.data_ptr() != ptr
+    assert model.mask_to_lengths(other, 2, 8)[0].tolist() == [5, 2]
+
+
+def test_inference_tensor_weights_are_refreshed_every_call():
+    """Parameters created under inference mode carry no version counter: the packed q/k/v copies
+    are refreshed in place on every call instead of trusting a cached version."""
+    cfg = TransformerConfig(1, 8, 16, 4, 32, 1, True)
+    with torch.inference_mode():
+        model = UserOptimizedTransformer(cfg)
+    att = model.layers[0].attention
+    assert att.k_proj.weight.is_inference()
+    assert model._weights_key() is None
+    packed = model.packed_weights()[0]
+    with torch.inference_mode():
+        att.k_proj.weight.add_(1.0)
+        att.q_proj.bias.mul_(2.0)
+    again = model.packed_weights()[0]
+    assert again is packed  # same storage: captured graphs stay valid
+    d = cfg.d_model
+    assert torch.equal(again.w_qkv[d:2 * d], att.k_proj.weight)
+    assert torch.equal(again.b_qkv[:d], att.q_proj.bias)
+
+
+def test_repacking_drops_graphs_of_every_shape():
+    model = UserOptimizedTransformer(TransformerConfig(1, 8, 16, 4, 32, 1, True))
+    model.packed_weights()
+    model._graphs[("a",)] = object()
+    model._graphs[("b",)] = object()
+    with torch.no_grad():
+        model.layers[0].ffn_in.bias.add_(1.0)
+    model.packed_weights()
+    assert model._graphs == {}

@@ -35,6 +35,7 @@ SIGNATURES = {
     "b2_abi_version": (ctypes.c_int, []),
     "b2_last_error": (ctypes.c_char_p, []),
     "b2_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int]),
+    "b2_device_status_async": (ctypes.c_int, [_vp, _vp]),
     "b2_layernorm_fwd": (
         ctypes.c_int,
         [_vp, ctypes.c_int, _vp, _vp, ctypes.c_float, _vp, _vp, _vp, _i64, _i64, _vp],
@@ -139,6 +140,54 @@ def device_status(clear: bool = True) -> int:
     out = ctypes.c_uint32(0)
     _check(lib.b2_device_status(ctypes.byref(out), 1 if clear else 0), "b2_device_status")
     return int(out.value)
+
+
+class StatusWatch:
+    """Checks every forward pass for a kernel pipeline timeout without synchronising.
+
+    `after_forward()` enqueues a copy of the device's status word into pinned host memory behind
+    the pass's kernels (b2_device_status_async) and records an event; `check()` reads the copy of
+    an earlier pass once its event has completed (never waiting for it unless `wait=True`) and
+    raises RuntimeError if a kernel gave up waiting, so a timed-out pass is reported at the latest
+    by the next call. The status word is sticky until cleared (b2_device_status(clear=1)), so a
+    timeout is never missed, only reported one call late when its copy has not landed yet.
+    """
+
+    def __init__(self) -> None:
+        self._host: Optional[torch.Tensor] = None
+        self._event: Optional[torch.cuda.Event] = None
+        self.status = 0
+
+    def check(self, wait: bool = False) -> int:
+        ev = self._event
+        if ev is None:
+            return 0
+        if not wait and not ev.query():
+            return 0
+        ev.synchronize()
+        self._event = None
+        value = int(self._host[0].item())
+        if value:
+            self.status = value
+            kernel, site, reason = value >> 16, (value >> 8) & 0xFF, value & 0xFF
+            names = {1: "layernorm", 2: "linear", 3: "attention", 4: "peer barrier"}
+            raise RuntimeError(
+                f"a {names.get(kernel, kernel)} kernel gave up waiting (status {value:#x}: site {site}, reason "
+                f"{reason}); outputs computed since then are not valid. Clear the status with "
+                "_capi.device_status(clear=True) after handling it")
+        return 0
+
+    def after_forward(self, device: torch.device) -> None:
+        if self._host is None:
+            self._host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        if self._event is not None and not self._event.query():
+            return  # the previous copy is still in flight: it will report the same sticky word
+        self._event = None
+        lib = load_library()
+        _check(lib.b2_device_status_async(self._host.data_ptr(), _stream_ptr(device)), "b2_device_status_async")
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(device))
+        self._event = ev
 
 
 def layernorm(

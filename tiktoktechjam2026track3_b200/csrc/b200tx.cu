@@ -115,6 +115,13 @@ B2_API int b2_device_status(uint32_t* out_status, int clear) {
   return 0;
 }
 
+B2_API int b2_device_status_async(uint32_t* host_dst, void* stream) {
+  if (host_dst == nullptr) return fail(1, "b2_device_status_async: host_dst is null");
+  return check_launch(cudaMemcpyFromSymbolAsync(host_dst, g_device_status, sizeof(uint32_t), 0,
+                                                cudaMemcpyDeviceToHost, static_cast<cudaStream_t>(stream)),
+                      "b2_device_status_async");
+}
+
 B2_API int b2_layernorm_fwd(const void* x, int x_is_bf16, const void* gamma, const void* beta, float eps, void* y,
                             float* resid_out, const uint8_t* row_mask, int64_t rows, int64_t d_model, void* stream) {
   if (x == nullptr || gamma == nullptr || beta == nullptr || y == nullptr)

@@ -75,15 +75,6 @@ class _PackedBlock:
                  "w_1", "b_1", "w_2", "b_2")
 
 
-def _param_key(t: torch.Tensor) -> Tuple[int, int]:
-    # A move or dtype change gives new storage (data_ptr); an in-place update bumps _version.
-    # Inference tensors (a model built under torch.inference_mode) carry no version counter.
-    try:
-        return (t.data_ptr(), t._version)
-    except RuntimeError:
-        return (t.data_ptr(), 0)
-
-
 class MaskLengths:
     """Turns the harness's valid-token mask into what the kernels take, with a one-entry cache.
 
@@ -96,7 +87,9 @@ class MaskLengths:
     masked kernels, which compute exactly what the unmasked ones do; a CPU mask is checked at once
     and an all-true one elided (as the reference candidate does, models.py:1137-1161).
     The result is reused while the same mask storage is passed with an unchanged version counter
-    (inference tensors carry no version counter and are re-derived on every call).
+    (inference tensors carry no version counter and are re-derived on every call). The cache entry
+    holds the mask tensor itself, so its storage cannot be freed and handed to a different mask
+    while the entry could still match it.
     """
 
     _MESSAGE = "valid_token_mask must mark a prefix of each sequence (the form generate_random_case produces)"
@@ -120,7 +113,7 @@ class MaskLengths:
         if versioned:
             key = (m.data_ptr(), m._version, tuple(m.shape), tuple(m.stride()), m.device)
             if self._cache is not None and self._cache[0] == key:
-                return self._cache[1]
+                return self._cache[2]
         lengths = m.sum(dim=1, dtype=torch.int32)
         positions = torch.arange(seq_len, device=m.device, dtype=torch.int32)
         prefix = positions[None, :] < lengths[:, None]
@@ -140,7 +133,7 @@ class MaskLengths:
             else:
                 result = (lengths.contiguous(), m.reshape(-1).contiguous().view(torch.uint8))
         if versioned:
-            self._cache = (key, result)
+            self._cache = (key, m, result)
         return result
 
     def raise_if_invalid(self) -> None:
@@ -169,6 +162,7 @@ class UserOptimizedTransformer(nn.Module):
         self._packed: Optional[List[_PackedBlock]] = None
         self._packed_key: Optional[tuple] = None
         self._mask_lengths = MaskLengths()
+        self._status = _capi.StatusWatch()
         self._launch_log: Optional[list] = None
         # CUDA-graph replay of the per-block launches (launch amortisation only: the graph holds
         # exactly the kernels the eager path launches). Keyed by shape, device and mask presence.
@@ -202,8 +196,11 @@ class UserOptimizedTransformer(nn.Module):
             key.append((fp["weight"].data_ptr(), fp["weight"]._version))
             key.append((fp["bias"].data_ptr(), fp["bias"]._version))
         except RuntimeError:  # inference tensors have no version counter
-            return tuple(_param_key(p) for p in self.parameters())
+            return None
         return tuple(key)
+
+    def _storage_key(self) -> tuple:
+        return tuple(p.data_ptr() for p in self.parameters())
 
     def packed_weights(self) -> List[_PackedBlock]:
         """Per-block bf16 weights, with q/k/v packed into one [3D, D] projection (cached).
@@ -212,8 +209,19 @@ class UserOptimizedTransformer(nn.Module):
         [0, D) are q_proj, [D, 2D) k_proj, [2D, 3D) v_proj. Rebuilt when any parameter changes.
         """
         key = self._weights_key()
+        if key is None:
+            # Parameters created under torch.inference_mode carry no version counter, so an
+            # in-place update cannot be seen: the packed q/k/v copies (the only weights held as
+            # copies; every other packed tensor is the parameter itself) are refreshed in place on
+            # every call, which keeps captured graphs valid, and storage changes repack.
+            skey = ("storage",) + self._storage_key()
+            if self._packed is not None and self._packed_key == skey:
+                self._refresh_qkv_copies()
+                return self._packed
+            key = skey
         if self._packed is not None and self._packed_key == key:
             return self._packed
+        self._graphs.clear()  # graphs replay the packed tensors they were captured with
         packed = []
         with torch.no_grad():
             for layer in self.layers:
@@ -230,6 +238,15 @@ class UserOptimizedTransformer(nn.Module):
         self._packed = packed
         self._packed_key = key
         return packed
+
+    def _refresh_qkv_copies(self) -> None:
+        with torch.no_grad():
+            for layer, pb in zip(self.layers, self._packed):
+                att = layer.attention
+                d = att.d_model
+                for i, lin in enumerate((att.q_proj, att.k_proj, att.v_proj)):
+                    pb.w_qkv[i * d:(i + 1) * d].copy_(lin.weight)
+                    pb.b_qkv[i * d:(i + 1) * d].copy_(lin.bias)
 
     # ------------------------------------------------------------------ masks
     def mask_to_lengths(
@@ -298,9 +315,12 @@ class UserOptimizedTransformer(nn.Module):
         # first kernel. The launches use the packed weights of the previous call (memory they keep
         # alive, on x's device); if the parameters changed since then, the weights are repacked and
         # the pass runs again, and the stale result is never returned.
+        # A kernel of an earlier call that gave up waiting (status word, read without a sync).
+        self._status.check()
         packed = self._packed
         speculative = (packed is not None and packed[0].w_qkv.device == x.device
-                       and packed[0].w_qkv.dtype == torch.bfloat16)
+                       and packed[0].w_qkv.dtype == torch.bfloat16 and self._packed_key is not None
+                       and self._packed_key[0] != "storage")
         if not speculative:
             packed = self._checked_packed(x.device)
         kv_len, row_mask = self.mask_to_lengths(valid_token_mask, batch, seq_len)
@@ -309,8 +329,15 @@ class UserOptimizedTransformer(nn.Module):
         if speculative and self._weights_key() != self._packed_key:
             packed = self._checked_packed(x.device)
             out = self._forward_tokens(xc, batch, seq_len, kv_len, row_mask, packed)
+        self._status.after_forward(x.device)
         self._mask_lengths.raise_if_invalid()
         return out
+
+    def check_device_status(self) -> None:
+        """Waits for the last forward pass and raises RuntimeError if any of its kernels (or an
+        earlier one) gave up waiting; forward() itself reports this, without waiting, at the
+        latest on the call after the one that timed out."""
+        self._status.check(wait=True)
 
     def _checked_packed(self, device: torch.device) -> List[_PackedBlock]:
         packed = self.packed_weights()

@@ -100,6 +100,36 @@ def tp_shard_state(state: Dict[str, torch.Tensor], config, world: int, rank: int
     return out
 
 
+def _check_status(plan) -> None:
+    """Raises if a kernel of an earlier call gave up waiting. A timed-out flag barrier can leave a
+    signal set in a pad, so later barriers would pair up one step out of order: the plan drops its
+    symmetric-memory buffers (pads included) and refuses to run until `reset()` has been called on
+    every rank, which re-creates them zeroed behind a barrier of the process group."""
+    if plan._failed:
+        raise RuntimeError(f"{type(plan).__name__}: an earlier call timed out on the device (status "
+                           f"{plan._failed:#x}); call reset() on every rank before the next forward")
+    try:
+        plan._status.check()
+    except RuntimeError:
+        plan._failed = plan._status.status or 1
+        plan.close()
+        raise
+
+
+def _reset(plan) -> None:
+    """Clears a failed plan on this rank (every rank calls it): waits for the device, clears the
+    status word, drops the buffers and synchronises with the other ranks, so that the next call's
+    rendezvous allocates fresh, zeroed flag pads on all of them."""
+    import torch.distributed as dist
+
+    torch.cuda.synchronize(plan.device)
+    _capi.device_status(clear=True)
+    plan.close()
+    plan._failed = 0
+    plan._status = _capi.StatusWatch()
+    dist.barrier(group=plan.group)
+
+
 class TensorParallelTransformer:
     """Forward pass of the stack with heads/FFN columns split over a process group.
 
@@ -131,6 +161,10 @@ class TensorParallelTransformer:
             raise ValueError(f"collective must be 'auto', 'rs' or 'nccl', not {collective!r}")
         self.collective = collective
         self._symm_rs: Optional[dict] = None
+        self._status = _capi.StatusWatch()
+        self._failed = 0
+
+    reset = _reset
 
     def record_launches(self, enabled: bool) -> None:
         """When enabled, every kernel launch and all-reduce is bracketed by CUDA events."""
@@ -193,9 +227,13 @@ class TensorParallelTransformer:
         return self._symm_rs
 
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+        _check_status(self)
         if self.collective == "rs":
-            return self._forward_rs(x, valid_token_mask)
-        return self._forward_nccl(x, valid_token_mask)
+            out = self._forward_rs(x, valid_token_mask)
+        else:
+            out = self._forward_nccl(x, valid_token_mask)
+        self._status.after_forward(self.device)
+        return out
 
     def _forward_rs(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]) -> torch.Tensor:
         cfg = self.config
@@ -364,6 +402,10 @@ class ContextParallelTransformer:
         self._mask_lengths = MaskLengths()
         self._launch_log: Optional[list] = None
         self._buf: Optional[dict] = None
+        self._status = _capi.StatusWatch()
+        self._failed = 0
+
+    reset = _reset
 
     record_launches = TensorParallelTransformer.record_launches
     take_launch_log = TensorParallelTransformer.take_launch_log
@@ -403,6 +445,12 @@ class ContextParallelTransformer:
         _capi.peer_barrier(pads, self.rank, channel, self.device)
 
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+        _check_status(self)
+        out = self._forward_cp(x, valid_token_mask)
+        self._status.after_forward(self.device)
+        return out
+
+    def _forward_cp(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]) -> torch.Tensor:
         cfg = self.config
         if not x.is_cuda or x.dtype != torch.bfloat16:
             raise RuntimeError("ContextParallelTransformer needs a bf16 CUDA input")
