@@ -402,6 +402,24 @@ __device__ __forceinline__ void tmem_load_32cols(uint32_t taddr, float* v) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// The two halves of tmem_load_32cols, so that the next chunk's load is in flight while the
+// current one is processed: tmem_ld32_issue starts the load (the registers are not valid yet) and
+// tmem_ld32_wait waits for every tcgen05.ld this thread has issued. The wait takes the registers
+// as in-out operands, so no use of them can be scheduled before it.
+__device__ __forceinline__ void tmem_ld32_issue(uint32_t taddr, uint32_t (&r)[32]) {
+  __syncwarp();
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32_wait(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31]) : : "memory");
+}
+
 // 64 consecutive fp32 columns of this thread's TMEM lane in one instruction (then wait).
 __device__ __forceinline__ void tmem_load_64cols(uint32_t taddr, float* v) {
   uint32_t r[64];
@@ -616,6 +634,48 @@ __device__ __forceinline__ uint64_t splat2(float v) {
   uint64_t x;
   asm("mov.b64 %0, {%1, %1};" : "=l"(x) : "f"(v));
   return x;
+}
+
+__device__ __forceinline__ uint64_t pack2f(float a, float b) {
+  uint64_t x;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(a), "f"(b));
+  return x;
+}
+__device__ __forceinline__ void unpack2f(uint64_t x, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(x));
+}
+__device__ __forceinline__ uint64_t mul2f(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t fma2f(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
+// gelu_erf of two values with packed fp32x2 multiplies and FMAs (one instruction for both values):
+// the same Abramowitz & Stegun 7.1.26 evaluation, the polynomial carried negated so that
+// erf(|z|) = fma(-poly, e, 1) needs no negation, and the final 0.5 x (1 + sign(x) erf(|z|)) as
+// fma(0.5 x, s, 0.5 x) (one rounding fewer than the scalar form; both sit far below the bf16
+// rounding that follows).
+__device__ __forceinline__ void gelu_erf2(float& a, float& b) {
+  const uint64_t z = mul2f(pack2f(fabsf(a), fabsf(b)), splat2(0.70710678118654752440f));
+  float d0, d1;
+  unpack2f(fma2f(z, splat2(0.3275911f), splat2(1.0f)), d0, d1);
+  const uint64_t t = pack2f(fast_rcp(d0), fast_rcp(d1));
+  uint64_t pn = fma2f(t, splat2(-1.061405429f), splat2(1.453152027f));
+  pn = fma2f(t, pn, splat2(-1.421413741f));
+  pn = fma2f(t, pn, splat2(0.284496736f));
+  pn = fma2f(t, pn, splat2(-0.254829592f));
+  pn = mul2f(pn, t);
+  float q0, q1;
+  unpack2f(mul2f(z, mul2f(z, splat2(-1.44269504088896340736f))), q0, q1);
+  float e0, e1;
+  unpack2f(fma2f(pn, pack2f(fast_exp2(q0), fast_exp2(q1)), splat2(1.0f)), e0, e1);
+  const uint64_t h = mul2f(pack2f(a, b), splat2(0.5f));
+  unpack2f(fma2f(h, pack2f(copysignf(e0, a), copysignf(e1, b)), h), a, b);
 }
 
 __device__ __forceinline__ float fast_exp2(float x) {

@@ -163,24 +163,6 @@ __host__ __device__ constexpr bool epi_reads_residual() {
   return EPI == kEpiResidual || EPI == kEpiResidualZero;
 }
 
-// The global-memory operands of one 32-column chunk: the bias of the lane's 4 columns and, for the
-// residual epilogues, the lane's 8 residual row segments (kept rows). Issued one chunk ahead of
-// their use, so their L2 latency overlaps the previous chunk's work.
-template <int EPI>
-__device__ __forceinline__ void gemm_epi_fetch(const GemmParams& p, int row0, int col0, uint32_t keep, float4& b,
-                                               float4 (&res)[8]) {
-  const int lane = threadIdx.x & 31;
-  const int col = col0 + 4 * (lane & 7);
-  b = load_bias4(p.bias, col);
-  if constexpr (epi_reads_residual<EPI>()) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-      if ((keep >> i) & 1u)
-        res[i] = *reinterpret_cast<const float4*>(static_cast<const float*>(p.out) +
-                                                  static_cast<int64_t>(row0 + i * 4 + (lane >> 3)) * p.ldo + col);
-  }
-}
-
 // TMEM gives each lane one row of the accumulator, so a lane writing its own row would make every
 // warp-wide global access touch 32 different rows. The warp therefore passes its 32 x 32 fp32 chunk
 // through 4 KB of shared memory: row `lane` as 8 float4 pieces, the piece index XOR-swizzled by the
@@ -258,45 +240,178 @@ __device__ __forceinline__ void gemm_epi_store(const GemmParams& p, int row0, in
   }
 }
 
+// The operands of one warp's epilogue that do not depend on the accumulator: the row flags, the
+// bias of every chunk of the warp's columns and, for the residual epilogues, the residual rows of
+// its first chunk. They are loaded before the warp waits for the accumulator, so their latency
+// (a DRAM round trip for the bias right after the weights change, an L2 one otherwise) hides
+// behind the main loop instead of stalling each chunk. A per-CTA trace of C2's GEMMs
+// (%globaltimer stamps; 128 x 256 GELU tile) had the epilogue at 8.6 us against a 4.6 us main loop
+// while each chunk waited for its bias load and its TMEM load in turn.
+template <int BN, int EPI>
+struct EpiPrefetch {
+  uint32_t live, keep;
+  float4 bias[BN / 64];
+  float4 res[8];
+};
+
+template <int EPI>
+__device__ __forceinline__ void gemm_epi_fetch_residual(const GemmParams& p, int row0, int col0, uint32_t keep,
+                                                        float4 (&res)[8]) {
+  const int lane = threadIdx.x & 31;
+  const int col = col0 + 4 * (lane & 7);
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if ((keep >> i) & 1u)
+      res[i] = *reinterpret_cast<const float4*>(static_cast<const float*>(p.out) +
+                                                static_cast<int64_t>(row0 + i * 4 + (lane >> 3)) * p.ldo + col);
+}
+
+template <int BN, int EPI>
+__device__ __forceinline__ void gemm_epi_prefetch(const GemmParams& p, int row0, int n_blk, int half,
+                                                  EpiPrefetch<BN, EPI>& pre) {
+  gemm_epi_row_bits(p, row0, pre.live, pre.keep);
+  const int lane = threadIdx.x & 31;
+  const int c_begin = half * (BN / 64);
+#pragma unroll
+  for (int c = 0; c < BN / 64; ++c) {
+    const int col0 = n_blk * BN + (c_begin + c) * 32;
+    pre.bias[c] = col0 < p.N ? load_bias4(p.bias, col0 + 4 * (lane & 7)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  if constexpr (epi_reads_residual<EPI>()) {
+    if (n_blk * BN + c_begin * 32 < p.N) gemm_epi_fetch_residual<EPI>(p, row0, n_blk * BN + c_begin * 32, pre.keep,
+                                                                      pre.res);
+  }
+}
+
+// The bf16-output epilogues (bias, bias + GELU, bias + peer stores) of one tile for one warp. The
+// pointwise work runs in the TMEM layout (lane = row, 32 consecutive columns per chunk), the bias
+// read from shared memory as broadcasts, and only the bf16 results pass through the staging
+// buffer on their way to coalesced 16-byte row segments: half the shared-memory bytes of staging
+// the fp32 accumulator, which the tcgen05.mma of the next tile competes with for bandwidth (the
+// main loop ran ~1.4x slower under the fp32-staged epilogue in a per-CTA trace).
+// Staging layout per warp (4 KB): [0, 2 KB) the chunk's 32 rows x 64 B, 16-byte pieces XOR-swizzled
+// by (row / 2) % 4, so that both the row-wise stores and the transposed loads hit 32 distinct
+// banks per quarter-warp; [2 KB, +BN/2 x 4 B) the bias of the warp's columns.
+template <int BN, int EPI>
+__device__ __forceinline__ void gemm_epilogue_tile_bf16(const GemmParams& p, int row0, int n_blk, int half,
+                                                        uint32_t t_row, float4* stage, EpiPrefetch<BN, EPI>& pre) {
+  constexpr int kC = BN / 64;
+  const int lane = threadIdx.x & 31;
+  const int c_begin = half * kC;
+  int n_valid = 0;
+#pragma unroll
+  for (int c = 0; c < kC; ++c)
+    if (n_blk * BN + (c_begin + c) * 32 < p.N) n_valid = c + 1;
+  if (n_valid == 0) return;
+  uint4* rows = reinterpret_cast<uint4*>(stage);
+  float4* bias_s = stage + 128;
+  if (lane < 8) {
+#pragma unroll
+    for (int c = 0; c < kC; ++c) bias_s[c * 8 + lane] = pre.bias[c];
+  }
+  uint32_t buf[2][32];
+  tmem_ld32_issue(t_row + c_begin * 32, buf[0]);
+  __syncwarp();
+#pragma unroll
+  for (int c = 0; c < kC; ++c) {
+    if (c >= n_valid) break;
+    uint32_t(&cur)[32] = buf[c & 1];
+    tmem_ld32_wait(cur);
+    if (c + 1 < n_valid) tmem_ld32_issue(t_row + (c_begin + c + 1) * 32, buf[(c + 1) & 1]);
+    uint32_t pk[16];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 b = bias_s[c * 8 + j];
+      float x0 = __uint_as_float(cur[4 * j]) + b.x, x1 = __uint_as_float(cur[4 * j + 1]) + b.y;
+      float x2 = __uint_as_float(cur[4 * j + 2]) + b.z, x3 = __uint_as_float(cur[4 * j + 3]) + b.w;
+      if constexpr (EPI == kEpiBiasGelu) {
+        x0 = bf16_round(x0);
+        x1 = bf16_round(x1);
+        x2 = bf16_round(x2);
+        x3 = bf16_round(x3);
+        gelu_erf2(x0, x1);
+        gelu_erf2(x2, x3);
+      }
+      pk[2 * j] = pack_bf16x2(x0, x1);
+      pk[2 * j + 1] = pack_bf16x2(x2, x3);
+    }
+    const int sw = (lane >> 1) & 3;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      rows[lane * 4 + (q ^ sw)] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+    __syncwarp();
+    const int col0 = n_blk * BN + (c_begin + c) * 32;
+    const int piece = lane & 3;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = 8 * i + (lane >> 2);
+      const uint4 v = rows[r * 4 + (piece ^ ((r >> 1) & 3))];
+      const int row = row0 + r;
+      if (row < p.M) {
+        const int64_t off = static_cast<int64_t>(row) * p.ldo + col0 + 8 * piece;
+        *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + off) = v;
+        if constexpr (EPI == kEpiBiasPeers) {
+          if (col0 >= p.peer_col) {  // warp-uniform: a chunk's 32 columns are on one side
+            for (int rk = 0; rk < p.world; ++rk)
+              if (rk != p.rank) *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.peer_out[rk]) + off) = v;
+          }
+        }
+      }
+    }
+    __syncwarp();  // the staging rows are rewritten by the next chunk
+  }
+}
+
 // The epilogue of one tile for one warp: its TMEM lane quadrant (t_row) and its half of the tile's
-// columns, in 32-column chunks. The residual epilogues are software-pipelined: the next chunk's
-// bias and residual loads are issued as soon as the current chunk's have been consumed, so their
-// L2 latency overlaps this chunk's stores and the next chunk's TMEM load (C2's out_proj: 20.5 ->
-// 18.5 us per launch). The other epilogues load only the bias and keep the plain order (fetching it
-// a chunk ahead measured 2-3% slower on the large bias / GELU GEMMs, whose epilogue overlaps the
-// next tile's main loop anyway).
+// columns, in 32-column chunks, with the operands `pre` loaded before the accumulator was ready.
+// The next chunk's TMEM load is issued before the current chunk is processed (two register
+// buffers), and the residual epilogues fetch the next chunk's residual rows as soon as the current
+// ones are consumed, so each chunk's latencies overlap the previous chunk's work.
 template <int BN, int EPI>
 __device__ __forceinline__ void gemm_epilogue_tile(const GemmParams& p, int row0, int n_blk, int half, uint32_t t_row,
-                                                   float4* stage) {
-  uint32_t live, keep;
-  gemm_epi_row_bits(p, row0, live, keep);
-  const int c_begin = half * (BN / 64);
-  const int c_end = c_begin + BN / 64;
-  float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
-  float4 res[8];
-  if constexpr (epi_reads_residual<EPI>()) {
-    if (n_blk * BN + c_begin * 32 < p.N) gemm_epi_fetch<EPI>(p, row0, n_blk * BN + c_begin * 32, keep, b, res);
+                                                   float4* stage, EpiPrefetch<BN, EPI>& pre) {
+  if constexpr (EPI == kEpiBias || EPI == kEpiBiasGelu || EPI == kEpiBiasPeers) {
+    gemm_epilogue_tile_bf16<BN, EPI>(p, row0, n_blk, half, t_row, stage, pre);
+    return;
   }
-#pragma unroll 1
-  for (int c = c_begin; c < c_end; ++c) {
-    const int col0 = n_blk * BN + c * 32;
-    if (col0 >= p.N) break;  // warp-uniform
+  constexpr int kC = BN / 64;
+  const int c_begin = half * kC;
+  int n_valid = 0;  // chunks inside N (a prefix; warp-uniform)
+#pragma unroll
+  for (int c = 0; c < kC; ++c)
+    if (n_blk * BN + (c_begin + c) * 32 < p.N) n_valid = c + 1;
+  if (n_valid == 0) return;
+  // The residual epilogues hold a chunk of residual rows in registers as well: there each TMEM
+  // load is waited for at once (a second buffer made ptxas spill, and no register that a pending
+  // tcgen05.ld writes may be spilled), the others keep two buffers.
+  constexpr int kBufs = epi_reads_residual<EPI>() ? 1 : 2;
+  uint32_t buf[kBufs][32];
+  if (kBufs == 2) tmem_ld32_issue(t_row + c_begin * 32, buf[0]);
+#pragma unroll
+  for (int c = 0; c < kC; ++c) {
+    if (c >= n_valid) break;
+    uint32_t(&cur)[32] = buf[c % kBufs];
+    if (kBufs == 1) tmem_ld32_issue(t_row + (c_begin + c) * 32, cur);
+    tmem_ld32_wait(cur);
+    if (kBufs == 2 && c + 1 < n_valid) tmem_ld32_issue(t_row + (c_begin + c + 1) * 32, buf[(c + 1) % kBufs]);
+    const int col0 = n_blk * BN + (c_begin + c) * 32;
     {
       float acc[32];
-      tmem_load_32cols(t_row + c * 32, acc);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) acc[i] = __uint_as_float(cur[i]);
       gemm_epi_stage(acc, stage);
     }
     float4 v[8];
+    gemm_epi_gather(stage, pre.bias[c], v);
     if constexpr (epi_reads_residual<EPI>()) {
-      gemm_epi_gather(stage, b, v);
 #pragma unroll
       for (int i = 0; i < 8; ++i)
-        if ((keep >> i) & 1u) v[i] = make_float4(res[i].x + v[i].x, res[i].y + v[i].y, res[i].z + v[i].z, res[i].w + v[i].w);
-      if (c + 1 < c_end && col0 + 32 < p.N) gemm_epi_fetch<EPI>(p, row0, col0 + 32, keep, b, res);
-    } else {
-      gemm_epi_gather(stage, load_bias4(p.bias, col0 + 4 * (threadIdx.x & 7)), v);
+        if ((pre.keep >> i) & 1u)
+          v[i] = make_float4(pre.res[i].x + v[i].x, pre.res[i].y + v[i].y, pre.res[i].z + v[i].z,
+                             pre.res[i].w + v[i].w);
+      if (c + 1 < n_valid) gemm_epi_fetch_residual<EPI>(p, row0, col0 + 32, pre.keep, pre.res);
     }
-    gemm_epi_store<EPI>(p, row0, col0, v, live, keep);
+    gemm_epi_store<EPI>(p, row0, col0, v, pre.live, pre.keep);
     __syncwarp();  // the staging buffer is rewritten by the next chunk
   }
 }
@@ -645,9 +760,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int n_blk = tile % p.n_blocks;
       const int acc = local & 1;
       const uint32_t acc_ph = (local >> 1) & 1;
+      const int row = m_blk * kGemmBM + row_in_tile;
+      EpiPrefetch<BN, EPI> pre;
+      if constexpr (!is_ln_epi<EPI>()) gemm_epi_prefetch<BN, EPI>(p, row - lane, n_blk, half, pre);
       if (!mbar_wait(&acc_full[acc], acc_ph, abort_flag, kKernelGemm, 4)) break;
       tc_fence_after_sync();
-      const int row = m_blk * kGemmBM + row_in_tile;
       const uint32_t t_row =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * Cfg::kAccStride);
       if constexpr (is_ln_epi<EPI>()) {
@@ -725,7 +842,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       } else {
-        gemm_epilogue_tile<BN, EPI>(p, row - lane, n_blk, half, t_row, epi_stage);
+        gemm_epilogue_tile<BN, EPI>(p, row - lane, n_blk, half, t_row, epi_stage, pre);
       }
       tc_fence_before_sync();
       mbar_arrive(&acc_empty[acc]);
@@ -905,12 +1022,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       const int n_blk = tile % p.n_blocks;
       const int acc = local & 1;
       const uint32_t acc_ph = (local >> 1) & 1;
+      const int row = m_blk * 256 + row_in_tile;
+      EpiPrefetch<BN, EPI> pre;
+      gemm_epi_prefetch<BN, EPI>(p, row - lane, n_blk, half, pre);
       if (!mbar_wait(&acc_full[acc], acc_ph, abort_flag, kKernelGemm, 14)) break;
       tc_fence_after_sync();
-      const int row = m_blk * 256 + row_in_tile;
       const uint32_t t_row =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * Cfg::kAccStride);
-      gemm_epilogue_tile<BN, EPI>(p, row - lane, n_blk, half, t_row, epi_stage);
+      gemm_epilogue_tile<BN, EPI>(p, row - lane, n_blk, half, t_row, epi_stage, pre);
       tc_fence_before_sync();
       mbar_arrive_cluster(acc ? acc_empty_leader1 : acc_empty_leader0);
     }

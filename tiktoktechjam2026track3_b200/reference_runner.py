@@ -47,11 +47,16 @@ REPO_ROOT = Path(__file__).resolve().parents[1]
 DEFAULT_INSTALL = REPO_ROOT / "baseline" / "_ref"
 
 # Runner tolerances (--atol, --rtol) under which the strict elementwise rule accepts this module
-# against the reference's bf16 baseline, per benchmark configuration: they have to admit the
-# bf16 baseline's own rounding error (up to ~0.11 absolute at 12 layers against fp32).
+# against the reference's bf16 baseline, per benchmark configuration. Measured on a B200 with the
+# runner's seeds (1234 + trial, 5 trials): at rtol 0.02 the largest |this - bf16 baseline| among
+# elements outside the relative band is 0.0156 (c1) and 0.109 (c2), while this module is within
+# 0.0037 of the fp32 result (normwise) and the bf16 baseline within 0.021 — the difference is the
+# baseline's own rounding (the c2 baseline alone fails the 2^-7 gate). The atol values leave a
+# margin of about 2x (c1) and 1.4x (c2) over those figures; the runner's defaults (0.002, 0.02)
+# fail 2.3 % (c1) and 13 % (c2) of the elements for the same reason.
 STRICT_RULE_TOLERANCES = {
-    "c1": (0.05, 0.05),
-    "c2": (0.125, 0.1),
+    "c1": (0.03, 0.02),
+    "c2": (0.15, 0.02),
 }
 
 
