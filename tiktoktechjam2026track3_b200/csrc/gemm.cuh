@@ -662,10 +662,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
+  const int num_tiles = p.m_blocks * p.n_blocks;
+  // The weights (B operand) do not depend on the previous kernel: the first ring's worth of W
+  // tiles is requested before waiting for it (programmatic dependent launch), so their DRAM
+  // latency overlaps the previous kernel's tail. A per-CTA trace showed the first stage landing
+  // ~2 us after the wait when both operands were requested only then.
+  int w_early = 0;
+  if (warp == 0 && lane == 0) {
+    for (int tile = blockIdx.x; tile < num_tiles && w_early < kStages; tile += gridDim.x) {
+      const int n_blk = tile % p.n_blocks;
+      for (int kb = 0; kb < p.k_blocks && w_early < kStages; ++kb, ++w_early) {
+        mbar_arrive_expect_tx(&full[w_early], Cfg::kStageBytes);
+        tma_load_2d(s_b + w_early * Cfg::kBBytes, &tm_b, &full[w_early], kb * kGemmBK, n_blk * BN);
+      }
+    }
+  }
   pdl_wait_previous_grid();
   pdl_allow_next_grid();
-
-  const int num_tiles = p.m_blocks * p.n_blocks;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -681,9 +694,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
+          if (issued >= w_early) {
+            mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
+            tma_load_2d(s_b + s * Cfg::kBBytes, &tm_b, &full[s], kb * kGemmBK, n_blk * BN);
+          }
           tma_load_2d(s_a + s * Cfg::kABytes, &tm_a, &full[s], kb * kGemmBK, m_blk * kGemmBM);
-          tma_load_2d(s_b + s * Cfg::kBBytes, &tm_b, &full[s], kb * kGemmBK, n_blk * BN);
           ++issued;
           if (++s == kStages) {
             s = 0;
@@ -692,6 +707,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
       if (!ok) {
+        // W tiles requested early for stages whose A tile was never issued: their barrier phase
+        // cannot complete, so give those copies a fixed time to land in shared memory.
+        if (w_early > issued) {
+          const uint64_t t0 = global_timer_ns();
+          while (global_timer_ns() - t0 < 200000ull) {
+          }
+        }
         // Let the copies still in flight (at most the last kStages issued) land before exit.
         int n = issued < kStages ? issued : kStages;
         int ss = s;
