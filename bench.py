@@ -381,7 +381,9 @@ def main() -> None:
     if world > 1:
         import torch.distributed as dist
 
-        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep stdout to the one JSON line
+        # NCCL writes its banner and log lines to stdout (even the version line at WARN): send them
+        # to stderr, so that stdout carries only the one JSON line.
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
 
     weak = args.per_gpu_batch > 0
