@@ -1,6 +1,7 @@
 // Flash-style multi-head self-attention forward: the shared parameters, the host entry point,
-// and the softmax wait helper. The tcgen05 kernel for head_dim 64 and 128 is in
-// attention_pair.cuh; head dims 8, 16, 32 and 256 run on CUDA cores (attention_simt.cuh).
+// and the softmax wait helper. The tcgen05 kernels are in attention_solo.cuh (head_dim 64, one
+// query tile per CTA, two CTAs per SM) and attention_pair.cuh (head_dim 128, two query tiles per
+// CTA); head dims 8, 16, 32 and 256 run on CUDA cores (attention_simt.cuh).
 //
 // Computes, per batch b, head h and query q (BaselineSelfAttention.forward,
 // transformer_benchmark/models.py:55-75):
@@ -74,6 +75,8 @@ template <int HD>
 static cudaError_t launch_attention_simt(const __nv_bfloat16* qkv, int64_t ld_qkv, const AttnParams& p,
                                          cudaStream_t stream);
 
+static cudaError_t launch_attention_solo(const CUtensorMap& tm, const AttnParams& p, cudaStream_t stream);
+
 cudaError_t launch_attention(const __nv_bfloat16* qkv, int64_t ld_qkv, int64_t q_col, int64_t k_col, int64_t v_col,
                              int64_t B, int64_t S, int64_t H, int64_t hd, const int32_t* kv_len, int causal,
                              float scale, __nv_bfloat16* ctx, int64_t ld_ctx, cudaStream_t stream,
@@ -121,7 +124,7 @@ cudaError_t launch_attention(const __nv_bfloat16* qkv, int64_t ld_qkv, int64_t q
   cudaError_t e = make_tmap_bf16_2d(&tm, qkv, static_cast<uint64_t>(ld_qkv), static_cast<uint64_t>(B * S),
                                     static_cast<uint64_t>(ld_qkv) * 2, 64, 128);
   if (e != cudaSuccess) return e;
-  if (hd == 64) return launch_attention_pair<64>(tm, p, stream);
+  if (hd == 64) return launch_attention_solo(tm, p, stream);
   return launch_attention_pair<128>(tm, p, stream);
 }
 

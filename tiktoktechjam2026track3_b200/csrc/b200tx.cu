@@ -21,6 +21,7 @@
 #include "gemm.cuh"
 #include "attention.cuh"
 #include "attention_pair.cuh"
+#include "attention_solo.cuh"
 #include "attention_simt.cuh"
 #include "peer.cuh"
 
