@@ -77,7 +77,8 @@ def test_official_case(cuda_device, case_id):
     perf = report.performance_block(base, ours, cfg, WARMUP, REPEATS, 1)
     acc = asdict(accuracy)
     acc.update(rtol=0.02, atol=0.002, rule="strict_less_than_or", against="oracle in bf16 (reference baseline)")
-    result = report.official_case_result(case_id, cfg, acc, perf, gate=gate)
+    gpus = [report.gpu_scaling_entry(1, perf["optimized"]["median_ms"], cfg.batch_size * cfg.seq_len)]
+    result = report.official_case_result(case_id, cfg, acc, perf, gate=gate, gpus=gpus)
     result["correctness_passed"] = gate.passed  # acceptance: the 2^-7 gate against fp32
     result["status"] = "succeeded" if gate.passed else "correctness_failed"
     result["failure_category"] = None if gate.passed else "correctness"

@@ -46,10 +46,9 @@ namespace b2 {
 
 template <int HD>
 struct AttnPairCfg {
-  // head_dim 64 (exponential-bound): 3 warpgroups — control (TMA, two UMMA issuers, a spare
-  // warp), softmax group 0, group 1 — with the launch's 384 x 168 registers split as control 72,
-  // softmax 216 (128 x 72 + 256 x 216 = 64512), so a softmax thread has room to run a quarter of
-  // its exponentials on the FMA pipe (kPolyPairs) next to its 128 scores.
+  // head_dim 64 (exponential-bound; used for launches long enough to run at the power cap): 3
+  // warpgroups — control (TMA, two UMMA issuers, a spare warp), softmax group 0, group 1 — with the
+  // launch's 384 x 168 registers split as control 72, softmax 216 (128 x 72 + 256 x 216 = 64512).
   // head_dim 128 (MMA and exponentials even): 11 warps, uniform 168 registers, all exponentials
   // on the exponential unit. Measured on B200: each choice is the faster one for its head_dim.
   static constexpr bool kSplitRegs = HD == 64;
@@ -58,7 +57,10 @@ struct AttnPairCfg {
   static constexpr int kLaunchRegs = 168;
   static constexpr int kCtrlRegs = 72;
   static constexpr int kSoftmaxRegs = 216;
-  static constexpr int kPolyPairs = kSplitRegs ? 0x8 : 0x0;  // bit k: pair k of every 4 on the FMA pipe
+  // bit k: pair k of every 4 on the FMA pipe. 0 everywhere: the head_dim-64 one-tile kernel
+  // (attention_solo.cuh) takes every exponential on the exponential unit, and both head_dim-64
+  // kernels must give the same bits, whichever the launch size selects.
+  static constexpr int kPolyPairs = 0x0;
   static constexpr int kBoxBytes = 128 * 128;          // 128 rows x 64 bf16 columns (one TMA box)
   static constexpr int kBoxes = HD / 64;               // boxes per 128-row tile
   static constexpr int kQBytes = kBoxes * kBoxBytes;   // one 128 x HD query tile

@@ -25,8 +25,10 @@
 // Measured on one B200 against the two-tile kernel (CUDA events, L2 flushed): C2's attention
 // (B=8, S=512, 12 heads, padded) 33.3 -> 28.3 us, B=16 S=2048 causal 321 -> 254 us, B=1 S=16384
 // causal 871 -> 743 us (631 -> 740 TFLOP/s): two softmax warps per SM sub-partition keep the
-// exponential unit busier than the two-tile kernel's ping-pong between its groups, so it is the
-// head_dim-64 kernel for every shape. Same arithmetic per query tile as the two-tile kernel.
+// exponential unit busier than the two-tile kernel's ping-pong between its groups. Launches long
+// enough to hold the GPU at its power cap use the two-tile kernel instead (attention.cuh,
+// attention_prefers_pairs). Same arithmetic per query tile as the two-tile kernel, so the choice
+// never changes results.
 #pragma once
 #include "b2_common.cuh"
 #include "attention.cuh"

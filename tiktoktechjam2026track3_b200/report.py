@@ -5,8 +5,14 @@ Mirrors transformer_benchmark/runner.py: `official_case_result` (:423-441),
 `environment_metadata` (:210-220) and the timing block of `benchmark_models`
 (transformer_benchmark/timing.py:101-195), so that tools reading the reference's result files
 (e.g. its `benchmarkctl` validators) read this build's files too. Added keys are additive only:
-`"gate"` (the acceptance tolerance, max|y - r| <= 2^-7 max|r|) next to `"accuracy"`, and per-case
-`"implementation"` naming what produced the numbers.
+`"gate"` (the acceptance tolerance, max|y - r| <= 2^-7 max|r|) next to `"accuracy"`, per-case
+`"implementation"` naming what produced the numbers, and the multi-GPU / roofline / CPU-baseline
+records of this build: per case `"gpus"` (one entry per GPU count: `gpus`, `tokens_per_s`,
+`ms_per_iter`, `scaling`), `"roofline"` (the dominant kernel: `kernel`, `bound`, `achieved`,
+`peak`, `unit`, `frac`) and `"cpu_baseline"` (`cores`, `ms`, `tokens_per_s`, `kind`, `sample`);
+per document `"gpus"` (the largest GPU count of any case). The reference's readers ignore keys
+they do not know (its validator, orchestrator/crates/benchmarkctl/src/main.rs:1155-1240, checks only
+the keys it needs), so every document stays a valid schema-2 result.
 """
 
 from __future__ import annotations
@@ -61,12 +67,40 @@ def performance_block(baseline_ms: Optional[Sequence[float]], optimized_ms: Sequ
     }
 
 
+def gpu_scaling_entry(gpus: int, ms_per_iter: float, tokens_per_call: int, scaling: str = "strong") -> Dict[str, object]:
+    """One GPU count's throughput record: the configuration's B*S tokens per call over the
+    multi-GPU step time (max over ranks)."""
+    if gpus < 1 or not ms_per_iter > 0:
+        raise ValueError("gpus must be >= 1 and ms_per_iter positive")
+    if scaling not in ("strong", "weak"):
+        raise ValueError("scaling is 'strong' (fixed global batch) or 'weak' (fixed per-GPU batch)")
+    return {"gpus": int(gpus), "tokens_per_s": tokens_per_call * 1000.0 / ms_per_iter, "ms_per_iter": float(ms_per_iter),
+            "scaling": scaling}
+
+
+def roofline_entry(kernel: str, bound: str, achieved: float, peak: float, unit: str) -> Dict[str, object]:
+    """The dominant kernel against its roofline (tensor: TFLOP/s against the bf16 peak; hbm: GB/s
+    against the copy bandwidth)."""
+    if bound not in ("tensor", "hbm"):
+        raise ValueError("bound is 'tensor' or 'hbm'")
+    return {"kernel": kernel, "bound": bound, "achieved": float(achieved), "peak": float(peak), "unit": unit,
+            "frac": float(achieved) / float(peak)}
+
+
+def cpu_baseline_entry(cores: int, ms: float, tokens_per_call: int, kind: str, sample: str) -> Dict[str, object]:
+    """The reference computation timed on the host CPU (kind "reference" or "port")."""
+    return {"cores": int(cores), "ms": float(ms), "tokens_per_s": tokens_per_call * 1000.0 / ms, "kind": kind,
+            "sample": sample}
+
+
 def _plain(obj):
     return asdict(obj) if is_dataclass(obj) else obj
 
 
 def official_case_result(case_id: int, config: TransformerConfig, accuracy, performance: Optional[Dict[str, object]],
-                         gate=None, implementation: str = "tiktoktechjam2026track3_b200") -> Dict[str, object]:
+                         gate=None, implementation: str = "tiktoktechjam2026track3_b200",
+                         gpus: Optional[List[Dict[str, object]]] = None, roofline: Optional[Dict[str, object]] = None,
+                         cpu_baseline: Optional[Dict[str, object]] = None) -> Dict[str, object]:
     acc = _plain(accuracy)
     passed = bool(acc["passed"])
     result: Dict[str, object] = {
@@ -81,6 +115,12 @@ def official_case_result(case_id: int, config: TransformerConfig, accuracy, perf
     }
     if gate is not None:
         result["gate"] = _plain(gate)
+    if gpus is not None:
+        result["gpus"] = sorted(gpus, key=lambda e: e["gpus"])
+    if roofline is not None:
+        result["roofline"] = roofline
+    if cpu_baseline is not None:
+        result["cpu_baseline"] = cpu_baseline
     return result
 
 
@@ -123,9 +163,11 @@ def matrix_document(requested_case_ids: List[int], case_results: List[Dict[str, 
         correctness_passed, failure_category = True, None
     else:
         correctness_passed, failure_category = False, "correctness"
+    counts = [e["gpus"] for r in case_results for e in (r.get("gpus") or [])]
     return {
         "schema_version": SCHEMA_VERSION,
         "mode": "official_matrix",
+        "gpus": max(counts) if counts else 1,
         "case_set": CASE_SET,
         "requested_case_ids": list(requested_case_ids),
         "complete": complete,
