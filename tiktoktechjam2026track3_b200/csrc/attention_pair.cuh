@@ -125,12 +125,14 @@ __global__ void __launch_bounds__(AttnPairCfg<HD>::kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int b = blockIdx.x / p.H;
-  const int h = blockIdx.x % p.H;
+  int bh, cta_row;
+  attn_cta_coords(p, bh, cta_row);
+  const int b = bh / p.H;
+  const int h = bh % p.H;
   const int tpc = p.tiles_per_cta;  // query tiles per CTA: 2, or 1 with group 1 idle
   const int range_pairs[2] = {(p.n_q_tiles[0] + tpc - 1) / tpc, (p.n_q_tiles[1] + tpc - 1) / tpc};
   int y_local;
-  const int rg = attn_range_of(p, static_cast<int>(blockIdx.y), range_pairs, y_local);
+  const int rg = attn_range_of(p, cta_row, range_pairs, y_local);
   const int pair = range_pairs[rg] - 1 - y_local;  // heaviest causal pairs first
   const int q_tile0 = p.q_tile0[rg];
   const int q_end = p.q_end[rg];
@@ -544,7 +546,8 @@ static cudaError_t launch_attention_pair(const CUtensorMap& tm, const AttnParams
   AttnParams q = p;
   q.tiles_per_cta = attention_pair_tiles_per_cta(p, device_sm_count(dev));
   const int t = q.tiles_per_cta;
-  dim3 grid(p.B * p.H, (p.n_q_tiles[0] + t - 1) / t + (p.n_ranges > 1 ? (p.n_q_tiles[1] + t - 1) / t : 0));
+  const dim3 grid = attn_grid(q, static_cast<unsigned>((p.n_q_tiles[0] + t - 1) / t +
+                                                       (p.n_ranges > 1 ? (p.n_q_tiles[1] + t - 1) / t : 0)));
   return launch_pdl(attention_pair_kernel<HD>, grid, dim3(Cfg::kThreads), Cfg::kSmemBytes, stream, tm, q);
 }
 

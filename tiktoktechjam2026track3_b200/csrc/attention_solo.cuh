@@ -77,10 +77,12 @@ __global__ void __launch_bounds__(AttnSoloCfg::kThreads, 2)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int b = blockIdx.x / p.H;
-  const int h = blockIdx.x % p.H;
+  int bh, cta_row;
+  attn_cta_coords(p, bh, cta_row);
+  const int b = bh / p.H;
+  const int h = bh % p.H;
   int y_local;
-  const int rg = attn_range_of(p, static_cast<int>(blockIdx.y), p.n_q_tiles, y_local);
+  const int rg = attn_range_of(p, cta_row, p.n_q_tiles, y_local);
   const int tile = p.n_q_tiles[rg] - 1 - y_local;  // heaviest causal tiles first
   const int qt = p.q_tile0[rg] + tile;               // absolute query tile
   const int q_end = p.q_end[rg];
@@ -360,7 +362,7 @@ static cudaError_t launch_attention_solo(const CUtensorMap& tm, const AttnParams
   if (attr_err != cudaSuccess) return attr_err;
   AttnParams q = p;
   q.tiles_per_cta = 1;
-  dim3 grid(p.B * p.H, p.n_q_tiles[0] + (p.n_ranges > 1 ? p.n_q_tiles[1] : 0));
+  const dim3 grid = attn_grid(q, static_cast<unsigned>(p.n_q_tiles[0] + (p.n_ranges > 1 ? p.n_q_tiles[1] : 0)));
   return launch_pdl(attention_solo_kernel, grid, dim3(Cfg::kThreads), Cfg::kSmemBytes, stream, tm, q);
 }
 
