@@ -64,6 +64,33 @@ int b2_device_status(uint32_t* out_status, int clear);
  * has completed. No counterpart in the reference (its kernels have no bounded waits). */
 int b2_device_status_async(uint32_t* host_dst, void* stream);
 
+/* Sets the current device's limit for one pipeline wait (mbarrier, peer flag) in nanoseconds;
+ * 0 restores the default of 4 s, values below 1 ms are rejected. Applies to kernels launched after
+ * the call (synchronous copy to the device). No counterpart in the reference. */
+int b2_set_wait_limit(uint64_t limit_ns);
+
+/* Test-only fault selector of the current device, for checking the bounded waits without
+ * faulting the GPU: 0 = none (default); 1 = in the next b2_linear_fwd launches with one-CTA tiles,
+ * CTA 0's producer neither arms nor loads its first pipeline stage, so the MMA issuer's wait for
+ * it runs out after the wait limit: the kernel records status (2 << 16) | (3 << 8) | 1, leaves its
+ * loops, frees its tensor memory and returns; that CTA's output tile is not written. Reset to 0
+ * after use. No counterpart in the reference. */
+int b2_test_set_fault(int fault);
+
+/*
+ * The valid-token mask of a forward pass turned into what the kernels take, in one launch: the
+ * reference's padding masks are prefixes (generate_random_case, transformer_benchmark/cases.py:87-97),
+ * consumed as per-sequence key lengths by the attention (models.py:63-66) and as a row mask by the
+ * padded-row zeroing (models.py:78-79, 736-737, 917-918).
+ *   mask        [batch, seq_len] bool as bytes (0 / nonzero)
+ *   kv_len      [batch] int32 out: the number of nonzero entries of row b
+ *   row_mask_out [batch * seq_len] uint8 out (0 / 1), or NULL when the caller passes the mask
+ *               itself as the row mask
+ *   not_prefix  [batch] uint8 out: 1 where row b is not a prefix of length kv_len[b], else 0
+ */
+int b2_mask_lengths(const uint8_t* mask, int64_t batch, int64_t seq_len, int32_t* kv_len, uint8_t* row_mask_out,
+                    uint8_t* not_prefix, void* stream);
+
 /*
  * LayerNorm over the last dimension: y = (x - mean) / sqrt(var + eps) * gamma + beta, fp32
  * statistics, bf16 y. Replaces nn.LayerNorm in BaselineTransformerBlock (models.py:721, 723) and

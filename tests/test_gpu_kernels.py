@@ -441,3 +441,24 @@ def test_layernorm_gather_writes_every_copy():
     expect = torch.where(mask.bool()[:, None], expect, torch.zeros_like(expect))
     assert torch.equal(y0, y1)
     torch.testing.assert_close(y0.float(), expect, atol=1e-2, rtol=8e-3)
+
+
+# ---------------------------------------------------------------------------------- masks
+@pytest.mark.parametrize("batch,seq", [(8, 512), (3, 100), (1, 1), (64, 2048)])
+def test_mask_lengths_prefixes_and_non_prefixes(batch, seq):
+    g = _gen(batch * 7 + seq)
+    lengths = torch.randint(0, seq + 1, (batch,), device="cuda", generator=g)
+    mask = torch.arange(seq, device="cuda")[None, :] < lengths[:, None]
+    if batch > 2:
+        mask[1, seq - 1] = not bool(mask[1, seq - 1])  # row 1 breaks the prefix form unless full
+        if bool(mask[2, 0]):
+            mask[2, 0] = False  # a hole at the start
+    kv = torch.full((batch,), -7, device="cuda", dtype=torch.int32)
+    bad = torch.full((batch,), 9, device="cuda", dtype=torch.uint8)
+    copy = torch.zeros(batch * seq, device="cuda", dtype=torch.uint8)
+    _capi.mask_lengths(mask, kv, bad, copy)
+    torch.cuda.synchronize()
+    assert torch.equal(kv.long(), mask.sum(1))
+    prefix = torch.arange(seq, device="cuda")[None, :] < mask.sum(1)[:, None]
+    assert torch.equal(bad.bool(), (mask != prefix).any(1))
+    assert torch.equal(copy.view(batch, seq).bool(), mask)

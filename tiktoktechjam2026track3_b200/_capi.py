@@ -36,6 +36,9 @@ SIGNATURES = {
     "b2_last_error": (ctypes.c_char_p, []),
     "b2_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int]),
     "b2_device_status_async": (ctypes.c_int, [_vp, _vp]),
+    "b2_set_wait_limit": (ctypes.c_int, [ctypes.c_uint64]),
+    "b2_mask_lengths": (ctypes.c_int, [_vp, _i64, _i64, _vp, _vp, _vp, _vp]),
+    "b2_test_set_fault": (ctypes.c_int, [ctypes.c_int]),
     "b2_layernorm_fwd": (
         ctypes.c_int,
         [_vp, ctypes.c_int, _vp, _vp, ctypes.c_float, _vp, _vp, _vp, _i64, _i64, _vp],
@@ -140,6 +143,34 @@ def device_status(clear: bool = True) -> int:
     out = ctypes.c_uint32(0)
     _check(lib.b2_device_status(ctypes.byref(out), 1 if clear else 0), "b2_device_status")
     return int(out.value)
+
+
+def mask_lengths(mask: torch.Tensor, kv_len: torch.Tensor, not_prefix: torch.Tensor,
+                 row_mask_out: Optional[torch.Tensor] = None) -> None:
+    """kv_len[b] = valid keys of row b, not_prefix[b] = 1 where row b is not a prefix (see
+    b2_mask_lengths); mask is a contiguous bool [B, S] CUDA tensor."""
+    if mask.dtype != torch.bool or mask.dim() != 2:
+        raise ValueError("mask must be bool [batch, seq_len]")
+    _require(mask, torch.bool, "mask")
+    _require(kv_len, torch.int32, "kv_len")
+    _require(not_prefix, torch.uint8, "not_prefix")
+    batch, seq_len = mask.shape
+    if kv_len.numel() < batch or not_prefix.numel() < batch:
+        raise ValueError("kv_len and not_prefix need one entry per sequence")
+    if row_mask_out is not None:
+        _require(row_mask_out, torch.uint8, "row_mask_out")
+    _check(load_library().b2_mask_lengths(_ptr(mask), batch, seq_len, _ptr(kv_len), _ptr(row_mask_out),
+                                          _ptr(not_prefix), _stream_ptr(mask.device)), "b2_mask_lengths")
+
+
+def set_wait_limit(limit_ns: int = 0) -> None:
+    """Limit of one pipeline wait on the current device in ns (0 = the default 4 s)."""
+    _check(load_library().b2_set_wait_limit(int(limit_ns)), "b2_set_wait_limit")
+
+
+def test_set_fault(fault: int) -> None:
+    """Test-only fault selector (see b2_test_set_fault); 0 turns it off."""
+    _check(load_library().b2_test_set_fault(int(fault)), "b2_test_set_fault")
 
 
 class StatusWatch:

@@ -242,8 +242,9 @@ __global__ void __launch_bounds__(AttnPairCfg<HD>::kThreads, 1)
       if (!ok) {
         // Let copies in flight land: Q and the last (up to kStages) K and V tiles.
         const uint64_t t0 = global_timer_ns();
+        const uint64_t lim = wait_limit_ns();
         auto drain_wait = [&](uint64_t* bar, uint32_t par) {
-          while (!mbar_try_wait(bar, par) && global_timer_ns() - t0 < kWaitTimeoutNs) {
+          while (!mbar_try_wait(bar, par) && global_timer_ns() - t0 < lim) {
           }
         };
         drain_wait(q_full, 0);
@@ -347,7 +348,8 @@ __global__ void __launch_bounds__(AttnPairCfg<HD>::kThreads, 1)
       }
       umma_commit(&drain[t]);
       const uint64_t t0 = global_timer_ns();
-      while (!mbar_try_wait(&drain[t], 0) && global_timer_ns() - t0 < kWaitTimeoutNs) {
+      const uint64_t lim = wait_limit_ns();
+      while (!mbar_try_wait(&drain[t], 0) && global_timer_ns() - t0 < lim) {
       }
     }
    }

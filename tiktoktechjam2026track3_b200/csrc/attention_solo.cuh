@@ -164,8 +164,9 @@ __global__ void __launch_bounds__(AttnSoloCfg::kThreads, 2)
       if (!ok) {
         // Let copies in flight land: Q and the last (up to kStages) K and V tiles.
         const uint64_t t0 = global_timer_ns();
+        const uint64_t lim = wait_limit_ns();
         auto drain_wait = [&](uint64_t* bar, uint32_t par) {
-          while (!mbar_try_wait(bar, par) && global_timer_ns() - t0 < kWaitTimeoutNs) {
+          while (!mbar_try_wait(bar, par) && global_timer_ns() - t0 < lim) {
           }
         };
         drain_wait(q_full, 0);
@@ -238,7 +239,8 @@ __global__ void __launch_bounds__(AttnSoloCfg::kThreads, 2)
       }
       umma_commit(drain);
       const uint64_t t0 = global_timer_ns();
-      while (!mbar_try_wait(drain, 0) && global_timer_ns() - t0 < kWaitTimeoutNs) {
+      const uint64_t lim = wait_limit_ns();
+      while (!mbar_try_wait(drain, 0) && global_timer_ns() - t0 < lim) {
       }
     }
   } else {

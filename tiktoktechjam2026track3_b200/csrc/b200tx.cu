@@ -24,6 +24,7 @@
 #include "attention_solo.cuh"
 #include "attention_simt.cuh"
 #include "peer.cuh"
+#include "mask.cuh"
 
 #define B2_API extern "C" __attribute__((visibility("default")))
 
@@ -121,6 +122,32 @@ B2_API int b2_device_status_async(uint32_t* host_dst, void* stream) {
   return check_launch(cudaMemcpyFromSymbolAsync(host_dst, g_device_status, sizeof(uint32_t), 0,
                                                 cudaMemcpyDeviceToHost, static_cast<cudaStream_t>(stream)),
                       "b2_device_status_async");
+}
+
+B2_API int b2_set_wait_limit(uint64_t limit_ns) {
+  const uint64_t v = limit_ns == 0 ? kWaitTimeoutNs : limit_ns;
+  if (v < 1000000ull) return fail(1, "b2_set_wait_limit: limit below 1 ms");
+  return check_launch(cudaMemcpyToSymbol(g_wait_limit_ns, &v, sizeof(v)), "b2_set_wait_limit");
+}
+
+B2_API int b2_test_set_fault(int fault) {
+  if (fault < 0 || fault > static_cast<int>(kFaultGemmWithholdStage))
+    return fail(1, "b2_test_set_fault: unknown fault %d", fault);
+  const uint32_t v = static_cast<uint32_t>(fault);
+  return check_launch(cudaMemcpyToSymbol(g_test_fault, &v, sizeof(v)), "b2_test_set_fault");
+}
+
+B2_API int b2_mask_lengths(const uint8_t* mask, int64_t batch, int64_t seq_len, int32_t* kv_len, uint8_t* row_mask_out,
+                           uint8_t* not_prefix, void* stream) {
+  if (mask == nullptr || kv_len == nullptr || not_prefix == nullptr)
+    return fail(1, "b2_mask_lengths: null pointer argument");
+  if (batch < 0 || seq_len <= 0) return fail(1, "b2_mask_lengths: invalid shape batch=%lld seq_len=%lld",
+                                             (long long)batch, (long long)seq_len);
+  if (batch > 0x7fffffffLL || seq_len > 0x7fffffffLL) return fail(2, "b2_mask_lengths: dimension exceeds 2^31");
+  if (batch == 0) return 0;
+  return check_launch(launch_mask_lengths(mask, batch, seq_len, kv_len, row_mask_out, not_prefix,
+                                          static_cast<cudaStream_t>(stream)),
+                      "b2_mask_lengths");
 }
 
 B2_API int b2_layernorm_fwd(const void* x, int x_is_bf16, const void* gamma, const void* beta, float eps, void* y,

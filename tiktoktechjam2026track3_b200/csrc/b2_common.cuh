@@ -65,6 +65,17 @@ struct PollTimeout {
 // (the longest is an epilogue waiting for one full K loop); 4 s means the pipeline is stuck.
 constexpr uint64_t kWaitTimeoutNs = 4000000000ull;
 
+// The limit the kernels apply, settable from the host (b2_set_wait_limit) so that a test can make
+// a wait run out in milliseconds instead of seconds; kWaitTimeoutNs unless set.
+__device__ uint64_t g_wait_limit_ns = kWaitTimeoutNs;
+__device__ __forceinline__ uint64_t wait_limit_ns() { return *reinterpret_cast<volatile uint64_t*>(&g_wait_limit_ns); }
+
+// Test-only fault selector (b2_test_set_fault): 0 = none; kFaultGemmWithholdStage = the GEMM
+// producer of CTA 0 neither arms nor loads its first pipeline stage, so the MMA warp's wait for
+// that stage runs out (bounded, status word, abort) the way a lost TMA arrival would.
+constexpr uint32_t kFaultGemmWithholdStage = 1;
+__device__ uint32_t g_test_fault = 0;
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -150,7 +161,7 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits until the phase of `bar` with parity `parity` has completed. Returns false (after
-// recording a status word and raising *abort) when the wait exceeds kWaitTimeoutNs, and false
+// recording a status word and raising *abort) when the wait exceeds wait_limit_ns(), and false
 // without recording when another role of the CTA already raised *abort.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                           uint32_t kernel_id, uint32_t site) {
@@ -161,7 +172,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     if (mbar_try_wait(bar, parity)) return true;
     if ((++spins & 63u) == 0) {
       if (*abort) return false;
-      if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+      if (global_timer_ns() - t0 > wait_limit_ns()) {
         record_status(kernel_id, site, kReasonTimeout);
         *abort = 1;
         return false;
@@ -180,7 +191,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
     if (mbar_try_wait_cluster(bar, parity)) return true;
     if ((++spins & 63u) == 0) {
       if (*abort) return false;
-      if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+      if (global_timer_ns() - t0 > wait_limit_ns()) {
         record_status(kernel_id, site, kReasonTimeout);
         *abort = 1;
         return false;

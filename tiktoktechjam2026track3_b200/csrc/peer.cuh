@@ -11,7 +11,7 @@
 //   wait:   CAS 1 -> 0 (acquire, system scope) on this rank's slot for each source.
 // The flags reset themselves, so the barrier needs no epoch and replays unchanged inside a CUDA
 // graph. A signal that finds its slot still set waits until the peer has consumed the previous
-// one. Both waits are bounded (kWaitTimeoutNs): on expiry the kernel records a status and returns.
+// one. Both waits are bounded (wait_limit_ns()): on expiry the kernel records a status and returns.
 #pragma once
 
 #include "b2_common.cuh"
@@ -48,7 +48,7 @@ __global__ void __launch_bounds__(kMaxPeers, 1) peer_barrier_kernel(PeerPads pad
     const uint64_t t0 = global_timer_ns();
     bool ok = true;
     while (atom_cas_release_sys(to_peer, 0u, 1u) != 0u) {
-      if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+      if (global_timer_ns() - t0 > wait_limit_ns()) {
         record_status(kKernelPeerBarrier, 0, kReasonTimeout);
         ok = false;
         break;
@@ -57,7 +57,7 @@ __global__ void __launch_bounds__(kMaxPeers, 1) peer_barrier_kernel(PeerPads pad
     }
     if (ok) {
       while (atom_cas_acquire_sys(from_peer, 1u, 0u) != 1u) {
-        if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+        if (global_timer_ns() - t0 > wait_limit_ns()) {
           record_status(kKernelPeerBarrier, 1, kReasonTimeout);
           break;
         }

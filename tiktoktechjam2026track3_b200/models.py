@@ -97,6 +97,7 @@ class MaskLengths:
     def __init__(self) -> None:
         self._cache: Optional[tuple] = None
         self._flag: Optional[torch.Tensor] = None
+        self._flag_rows = 0
         self._pending: Optional[torch.cuda.Event] = None
 
     def __call__(
@@ -114,18 +115,24 @@ class MaskLengths:
             key = (m.data_ptr(), m._version, tuple(m.shape), tuple(m.stride()), m.device)
             if self._cache is not None and self._cache[0] == key:
                 return self._cache[2]
-        lengths = m.sum(dim=1, dtype=torch.int32)
-        positions = torch.arange(seq_len, device=m.device, dtype=torch.int32)
-        prefix = positions[None, :] < lengths[:, None]
         if m.is_cuda:
-            if self._flag is None:
-                self._flag = torch.zeros(1, dtype=torch.bool, pin_memory=True)
-            self._flag.copy_((m != prefix).any().view(1), non_blocking=True)
+            # One launch (b2_mask_lengths): per-sequence lengths and a per-row "not a prefix" byte,
+            # copied into pinned memory behind it; the mask bytes themselves are the row mask.
+            mc = m.contiguous()
+            lengths = torch.empty(batch, dtype=torch.int32, device=m.device)
+            verdict = torch.empty(batch, dtype=torch.uint8, device=m.device)
+            _capi.mask_lengths(mc, lengths, verdict)
+            if self._flag is None or self._flag.numel() < batch:
+                self._flag = torch.zeros(batch, dtype=torch.uint8, pin_memory=True)
+            self._flag[:batch].copy_(verdict, non_blocking=True)
+            self._flag_rows = batch
             self._pending = torch.cuda.Event()
             self._pending.record(torch.cuda.current_stream(m.device))
-            result: Tuple[Optional[torch.Tensor], Optional[torch.Tensor]] = (
-                lengths.contiguous(), m.reshape(-1).contiguous().view(torch.uint8))
+            result: Tuple[Optional[torch.Tensor], Optional[torch.Tensor]] = (lengths, mc.view(-1).view(torch.uint8))
         else:
+            lengths = m.sum(dim=1, dtype=torch.int32)
+            positions = torch.arange(seq_len, device=m.device, dtype=torch.int32)
+            prefix = positions[None, :] < lengths[:, None]
             if not torch.equal(m, prefix):
                 raise NotImplementedError(self._MESSAGE)
             if bool((lengths == seq_len).all()):
@@ -142,7 +149,7 @@ class MaskLengths:
         if ev is None:
             return
         ev.synchronize()
-        if bool(self._flag[0]):
+        if bool(self._flag[: self._flag_rows].any()):
             self._cache = None
             raise NotImplementedError(self._MESSAGE)
 
