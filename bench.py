@@ -277,11 +277,14 @@ def reference_path_record(cfg: TransformerConfig):
 def cpu_times(step, target_seconds: float, max_samples: int, min_samples: int = 1):
     """Runs `step` until target_seconds have passed (at least min_samples, at most max_samples),
     after one warm-up unless a single step is longer than a quarter of the target."""
-    t0 = time.perf_counter()
+    t_begin = t0 = time.perf_counter()
     step()
     first = time.perf_counter() - t0
     times = [] if first < target_seconds / 4 else [first]
-    t_begin = time.perf_counter()
+    if times:  # a single step already took a quarter of the budget: time from here on
+        t_begin = t0
+    else:
+        t_begin = time.perf_counter()
     while len(times) < max_samples and (len(times) < min_samples or time.perf_counter() - t_begin < target_seconds):
         t0 = time.perf_counter()
         step()
