@@ -24,10 +24,25 @@ __global__ void __launch_bounds__(kLnWarpsPerBlock * 32)
     layernorm_vec_kernel(const void* __restrict__ x_, const __nv_bfloat16* __restrict__ gamma,
                          const __nv_bfloat16* __restrict__ beta, float eps, __nv_bfloat16* __restrict__ y,
                          float* __restrict__ resid_out, const uint8_t* __restrict__ row_mask, int64_t rows) {
-  pdl_wait_previous_grid();
-  pdl_allow_next_grid();
   constexpr int D = NV * 128;
   const int lane = threadIdx.x & 31;
+  // gamma and beta are parameters, never written by the kernel this launch waits for: up to
+  // D = 2048 they are loaded before the programmatic-dependent-launch wait, so their latency
+  // overlaps the previous kernel's tail instead of following the row reductions (wider rows load
+  // them after the reductions, keeping the registers for the row).
+  constexpr bool kEarly = NV <= 16;
+  const uint2* gr = reinterpret_cast<const uint2*>(gamma);
+  const uint2* br = reinterpret_cast<const uint2*>(beta);
+  uint2 graw[NV], braw[NV];
+  if constexpr (kEarly) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      graw[i] = __ldg(gr + i * 32 + lane);
+      braw[i] = __ldg(br + i * 32 + lane);
+    }
+  }
+  pdl_wait_previous_grid();
+  pdl_allow_next_grid();
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kLnWarpsPerBlock + (threadIdx.x >> 5);
   if (row >= rows) return;
 
@@ -86,16 +101,16 @@ __global__ void __launch_bounds__(kLnWarpsPerBlock * 32)
   for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
   const float rstd = rsqrtf(q * (1.0f / D) + eps);
 
-  const uint2* gr = reinterpret_cast<const uint2*>(gamma);
-  const uint2* br = reinterpret_cast<const uint2*>(beta);
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
-    uint2 graw = __ldg(gr + i * 32 + lane);
-    uint2 braw = __ldg(br + i * 32 + lane);
-    __nv_bfloat162 g0 = *reinterpret_cast<__nv_bfloat162*>(&graw.x);
-    __nv_bfloat162 g1 = *reinterpret_cast<__nv_bfloat162*>(&graw.y);
-    __nv_bfloat162 b0 = *reinterpret_cast<__nv_bfloat162*>(&braw.x);
-    __nv_bfloat162 b1 = *reinterpret_cast<__nv_bfloat162*>(&braw.y);
+    if constexpr (!kEarly) {
+      graw[i] = __ldg(gr + i * 32 + lane);
+      braw[i] = __ldg(br + i * 32 + lane);
+    }
+    __nv_bfloat162 g0 = *reinterpret_cast<__nv_bfloat162*>(&graw[i].x);
+    __nv_bfloat162 g1 = *reinterpret_cast<__nv_bfloat162*>(&graw[i].y);
+    __nv_bfloat162 b0 = *reinterpret_cast<__nv_bfloat162*>(&braw[i].x);
+    __nv_bfloat162 b1 = *reinterpret_cast<__nv_bfloat162*>(&braw[i].y);
     const float o0 = fmaf((v[i][0] - mean) * rstd, __low2float(g0), __low2float(b0));
     const float o1 = fmaf((v[i][1] - mean) * rstd, __high2float(g0), __high2float(b0));
     const float o2 = fmaf((v[i][2] - mean) * rstd, __low2float(g1), __low2float(b1));
