@@ -1,8 +1,7 @@
 // Flash-style multi-head self-attention forward: the shared parameters, the host entry point,
 // and the softmax wait helper. The tcgen05 kernels are in attention_solo.cuh (head_dim 64, one
-// query tile per CTA, two CTAs per SM) and attention_pair.cuh (head_dim 128, and head_dim 64 in
-// launches long enough to run at the power cap: two query tiles per CTA); head dims 8, 16, 32 and
-// 256 run on CUDA cores (attention_simt.cuh).
+// query tile per CTA, two CTAs per SM) and attention_pair.cuh (head_dim 128, two query tiles per
+// CTA); head dims 8, 16, 32 and 256 run on CUDA cores (attention_simt.cuh).
 //
 // Computes, per batch b, head h and query q (BaselineSelfAttention.forward,
 // transformer_benchmark/models.py:55-75):
@@ -103,26 +102,6 @@ static cudaError_t launch_attention_simt(const __nv_bfloat16* qkv, int64_t ld_qk
 
 static cudaError_t launch_attention_solo(const CUtensorMap& tm, const AttnParams& p, cudaStream_t stream);
 
-// Score tiles (128 queries x 128 keys) a launch computes, masks applied.
-static long attention_tile_products(const AttnParams& p) {
-  long per_seq_max = 0;
-  for (int r = 0; r < p.n_ranges; ++r)
-    for (int t = 0; t < p.n_q_tiles[r]; ++t) {
-      const long qt = p.q_tile0[r] + t;
-      const long kv_tiles = (p.S + 127) / 128;
-      per_seq_max += p.causal ? (qt + 1 < kv_tiles ? qt + 1 : kv_tiles) : kv_tiles;
-    }
-  return per_seq_max * p.B * p.H;
-}
-
-// head_dim 64: the one-tile kernel (two CTAs per SM) is the faster one while the GPU runs at its
-// boost clock — C2 28 vs 33 us, B=16 S=2048 causal 254 vs 321 us, S=16384 causal 740 vs 631
-// TFLOP/s — but it streams every K/V tile once per query tile where the two-tile kernel streams it
-// once per pair, and in launches long enough to hold the GPU at its 1000 W power cap (the C5
-// sequences: 4 x 100000 tokens, ~140 ms per launch, SM clock ~1.3-1.7 GHz) that extra data
-// movement costs more clock than the scheduling gains: 572 vs 594 TFLOP/s measured there. Above
-// 4M score tiles per launch (about 6 ms at boost clock) the two-tile kernel is used.
-static bool attention_prefers_pairs(const AttnParams& p) { return attention_tile_products(p) > 4000000L; }
 
 cudaError_t launch_attention(const __nv_bfloat16* qkv, int64_t ld_qkv, int64_t q_col, int64_t k_col, int64_t v_col,
                              int64_t B, int64_t S, int64_t H, int64_t hd, const int32_t* kv_len, int causal,
@@ -172,8 +151,7 @@ cudaError_t launch_attention(const __nv_bfloat16* qkv, int64_t ld_qkv, int64_t q
   cudaError_t e = make_tmap_bf16_2d(&tm, qkv, static_cast<uint64_t>(ld_qkv), static_cast<uint64_t>(B * S),
                                     static_cast<uint64_t>(ld_qkv) * 2, 64, 128);
   if (e != cudaSuccess) return e;
-  if (hd == 64)
-    return attention_prefers_pairs(p) ? launch_attention_pair<64>(tm, p, stream) : launch_attention_solo(tm, p, stream);
+  if (hd == 64) return launch_attention_solo(tm, p, stream);
   return launch_attention_pair<128>(tm, p, stream);
 }
 

@@ -535,6 +535,9 @@ static int attention_pair_tiles_per_cta(const AttnParams& p, int sms) {
 
 template <int HD>
 static cudaError_t launch_attention_pair(const CUtensorMap& tm, const AttnParams& p, cudaStream_t stream) {
+  // Launched for head_dim 128 only; head_dim 64 runs on the one-tile kernel (attention_solo.cuh),
+  // measured faster at every benchmark size. The template's head_dim-64 configuration (register
+  // split, 4-stage rings) is not instantiated.
   using Cfg = AttnPairCfg<HD>;
   static std::once_flag once[64];
   int dev = 0;

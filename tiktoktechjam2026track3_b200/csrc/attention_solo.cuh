@@ -25,10 +25,11 @@
 // Measured on one B200 against the two-tile kernel (CUDA events, L2 flushed): C2's attention
 // (B=8, S=512, 12 heads, padded) 33.3 -> 28.3 us, B=16 S=2048 causal 321 -> 254 us, B=1 S=16384
 // causal 871 -> 743 us (631 -> 740 TFLOP/s): two softmax warps per SM sub-partition keep the
-// exponential unit busier than the two-tile kernel's ping-pong between its groups. Launches long
-// enough to hold the GPU at its power cap use the two-tile kernel instead (attention.cuh,
-// attention_prefers_pairs). Same arithmetic per query tile as the two-tile kernel, so the choice
-// never changes results.
+// exponential unit busier than the two-tile kernel's ping-pong between its groups. At C5 (4 x 100000
+// tokens, ~110 ms per launch at the 1000 W power cap) with the head-major grid order it runs at
+// 752 TFLOP/s against 672 for the two-tile kernel (692 without its register split): with K/V
+// served from L2, streaming them once per query tile no longer costs more than the scheduling
+// gains. It is the head_dim-64 kernel for every shape.
 #pragma once
 #include "b2_common.cuh"
 #include "attention.cuh"
@@ -290,7 +291,9 @@ __global__ void __launch_bounds__(AttnSoloCfg::kThreads, 2)
       }
       const uint64_t c2 = splat2(c);
       const uint64_t neg_mc2 = splat2(-m_ref * c);
-      float sum0 = 0.f, sum1 = 0.f;
+      // Row sums of the even and odd keys in the two halves of one packed add (the same per-lane
+      // rounding as two scalar sums).
+      uint64_t sum2 = 0;
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
         uint32_t w[16];
@@ -300,12 +303,13 @@ __global__ void __launch_bounds__(AttnSoloCfg::kThreads, 2)
           fma2_inplace(x0, x1, c2, neg_mc2);
           const float e0 = fast_exp2(x0);
           const float e1 = fast_exp2(x1);
-          sum0 += e0;
-          sum1 += e1;
+          sum2 = add2f(sum2, pack2f(e0, e1));
           w[k] = pack_bf16x2(e0, e1);
         }
         tmem_store_16cols_async(t_p + 16 * g, w);
       }
+      float sum0, sum1;
+      unpack2f(sum2, sum0, sum1);
       l_sum = l_sum * alpha + (sum0 + sum1);
       tmem_wait_st();
       if (__any_sync(0xffffffffu, alpha < 1.f)) {
