@@ -614,7 +614,7 @@ def main() -> None:
                 "padding_ratio": pad,
                 "parallelism": (f"cp{world} (each sequence's tokens in 2 x {world} zigzag chunks; Q/K/V rows "
                                 "all-gathered over NVLink into every GPU's full-length buffer, attention of the "
-                                "rank's query rows, LayerNorms and GEMMs on its own rows; 2 flag barriers per block)")
+                                "rank's query rows, LayerNorms and GEMMs on its own rows; 1 flag barrier per block)")
                 if split_sequences and model.collective == "cp" else
                 (f"tp{world} (heads / FFN columns; " + {
                     "rs": "out_proj / ffn_out GEMM epilogues add each row into its owner's fp32 residual over "

@@ -167,8 +167,9 @@ int b2_linear_ln_plan(int64_t m, int64_t n, int64_t k, int sm_count, int* tile_n
  * 128-row tiles are not written.
  *   qkv     [batch*seq_len, ld_qkv] bf16; head h of Q/K/V at columns q_col/k_col/v_col + h*head_dim
  *   kv_len  [batch] int32 (valid-key prefix length per sequence) or NULL (= seq_len)
- * Requires head_dim in {64, 128} (tcgen05 tensor cores; q/k/v_col multiples of 64) or in
- * {8, 16, 32, 256} (CUDA cores; q/k/v_col multiples of 8), ld_qkv % 8 == 0, an sm_100 device.
+ * Requires head_dim in {64, 128} (tcgen05 tensor cores; q/k/v_col multiples of 64), 32 (tensor
+ * cores; q/k/v_col multiples of 8) or {8, 16, 256} (CUDA cores; q/k/v_col multiples of 8),
+ * ld_qkv % 8 == 0, an sm_100 device.
  */
 int b2_attention_fwd(const void* qkv, int64_t ld_qkv, int64_t q_col, int64_t k_col, int64_t v_col, int64_t batch,
                      int64_t seq_len, int64_t num_heads, int64_t head_dim, const int32_t* kv_len, int causal,

@@ -1,7 +1,7 @@
 // Flash-style multi-head self-attention forward: the shared parameters, the host entry point,
-// and the softmax wait helper. The tcgen05 kernels are in attention_solo.cuh (head_dim 64, one
-// query tile per CTA, two CTAs per SM) and attention_pair.cuh (head_dim 128, two query tiles per
-// CTA); head dims 8, 16, 32 and 256 run on CUDA cores (attention_simt.cuh).
+// and the softmax wait helper. The tcgen05 kernels are in attention_solo.cuh (head_dim 32 and 64,
+// one query tile per CTA, two CTAs per SM) and attention_pair.cuh (head_dim 128, two query tiles
+// per CTA); head dims 8, 16 and 256 run on CUDA cores (attention_simt.cuh).
 //
 // Computes, per batch b, head h and query q (BaselineSelfAttention.forward,
 // transformer_benchmark/models.py:55-75):
@@ -100,6 +100,7 @@ template <int HD>
 static cudaError_t launch_attention_simt(const __nv_bfloat16* qkv, int64_t ld_qkv, const AttnParams& p,
                                          cudaStream_t stream);
 
+template <int HD>
 static cudaError_t launch_attention_solo(const CUtensorMap& tm, const AttnParams& p, cudaStream_t stream);
 
 
@@ -139,19 +140,18 @@ cudaError_t launch_attention(const __nv_bfloat16* qkv, int64_t ld_qkv, int64_t q
       return launch_attention_simt<8>(qkv, ld_qkv, p, stream);
     case 16:
       return launch_attention_simt<16>(qkv, ld_qkv, p, stream);
-    case 32:
-      return launch_attention_simt<32>(qkv, ld_qkv, p, stream);
     case 256:
       return launch_attention_simt<256>(qkv, ld_qkv, p, stream);
     default:
       break;
   }
-  if (hd != 64 && hd != 128) return cudaErrorInvalidValue;
+  if (hd != 32 && hd != 64 && hd != 128) return cudaErrorInvalidValue;
   CUtensorMap tm;
   cudaError_t e = make_tmap_bf16_2d(&tm, qkv, static_cast<uint64_t>(ld_qkv), static_cast<uint64_t>(B * S),
                                     static_cast<uint64_t>(ld_qkv) * 2, 64, 128);
   if (e != cudaSuccess) return e;
-  if (hd == 64) return launch_attention_solo(tm, p, stream);
+  if (hd == 32) return launch_attention_solo<32>(tm, p, stream);
+  if (hd == 64) return launch_attention_solo<64>(tm, p, stream);
   return launch_attention_pair<128>(tm, p, stream);
 }
 

@@ -53,10 +53,18 @@ struct AttnSoloCfg {
   static_assert(2 * (kSmemBytes + 1024) <= 233472, "two CTAs per SM");
 };
 
+// HD = 64, or 32 (the reference's official case matrix: D = 128 with 4 heads). At head_dim 32 every
+// tile is still loaded as a 64-column TMA box (the head's 32 columns and the next 32 of the packed
+// QKV row, zero-filled past its end): S = Q K^T takes only the first two 16-deep k-steps, i.e. this
+// head's columns, and O += P V is computed 64 wide, its second half (the neighbouring columns)
+// discarded — the exponentials, not the MMAs, bound the kernel, and the operand layouts stay the
+// 128-byte-swizzled ones of head_dim 64.
+template <int HD>
 __global__ void __launch_bounds__(AttnSoloCfg::kThreads, 2)
     attention_solo_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnParams p) {
+  static_assert(HD == 32 || HD == 64, "one-tile kernel: head_dim 32 or 64");
   using Cfg = AttnSoloCfg;
-  constexpr int HD = 64;
+  constexpr int kON = 64;  // columns of O (and width of the P V product)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* s_q = smem + Cfg::kOffQ;
@@ -181,7 +189,7 @@ __global__ void __launch_bounds__(AttnSoloCfg::kThreads, 2)
     // ---------------- UMMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc_bf16_f32(128, 128, 0, 0);
-      constexpr uint32_t idesc_o = make_idesc_bf16_f32(128, HD, 0, 1);
+      constexpr uint32_t idesc_o = make_idesc_bf16_f32(128, kON, 0, 1);
       const uint32_t q_addr = smem_u32(s_q);
       const uint32_t d_s = tmem_base + Cfg::kSCol;
       const uint32_t d_o = tmem_base + Cfg::kOCol;
@@ -316,7 +324,7 @@ __global__ void __launch_bounds__(AttnSoloCfg::kThreads, 2)
         // Rescale the accumulated output of the warp's rows (P(0..j-1) V, landed above); P(j) V is
         // not issued before p_full. Warp-uniform: the TMEM loads and stores are warp-collective.
 #pragma unroll 1
-        for (int cc = 0; cc < HD / 32; ++cc) {
+        for (int cc = 0; cc < kON / 32; ++cc) {
           float o[32];
           tmem_load_32cols(t_o + cc * 32, o);
 #pragma unroll
@@ -355,6 +363,7 @@ __global__ void __launch_bounds__(AttnSoloCfg::kThreads, 2)
   }
 }
 
+template <int HD>
 static cudaError_t launch_attention_solo(const CUtensorMap& tm, const AttnParams& p, cudaStream_t stream) {
   using Cfg = AttnSoloCfg;
   static std::once_flag once[64];
@@ -362,14 +371,14 @@ static cudaError_t launch_attention_solo(const CUtensorMap& tm, const AttnParams
   cudaGetDevice(&dev);
   cudaError_t attr_err = cudaSuccess;
   std::call_once(once[dev & 63], [&] {
-    attr_err = cudaFuncSetAttribute(attention_solo_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    attr_err = cudaFuncSetAttribute(attention_solo_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     Cfg::kSmemBytes);
   });
   if (attr_err != cudaSuccess) return attr_err;
   AttnParams q = p;
   q.tiles_per_cta = 1;
   const dim3 grid = attn_grid(q, static_cast<unsigned>(p.n_q_tiles[0] + (p.n_ranges > 1 ? p.n_q_tiles[1] : 0)));
-  return launch_pdl(attention_solo_kernel, grid, dim3(Cfg::kThreads), Cfg::kSmemBytes, stream, tm, q);
+  return launch_pdl(attention_solo_kernel<HD>, grid, dim3(Cfg::kThreads), Cfg::kSmemBytes, stream, tm, q);
 }
 
 }  // namespace b2

@@ -247,6 +247,8 @@ B2_API int b2_attention_rows_fwd(const void* qkv, int64_t ld_qkv, int64_t q_col,
   const bool tensor_core = head_dim == 64 || head_dim == 128;
   if (!tensor_core && head_dim != 8 && head_dim != 16 && head_dim != 32 && head_dim != 256)
     return fail(2, "b2_attention_rows_fwd: head_dim=%lld not supported (8, 16, 32, 64, 128, 256)", (long long)head_dim);
+  // 64 / 128: 64-column TMA boxes per head; 32 (also tensor cores, 64-column boxes starting at the
+  // head's 32-column offset) and the CUDA-core head dims: 16-byte aligned column offsets.
   const int64_t col_align = tensor_core ? 64 : 8;
   if (q_col % col_align || k_col % col_align || v_col % col_align || q_col < 0 || k_col < 0 || v_col < 0)
     return fail(2, "b2_attention_rows_fwd: q/k/v column offsets must be non-negative multiples of %lld",

@@ -377,9 +377,10 @@ class ContextParallelTransformer:
     [B*S, 3D] QKV buffer (torch symmetric memory), K and V also into every other rank's buffer —
     the all-gather of K and V, (n-1)/n of 2 bf16 [T, D] per GPU per layer, no reduction anywhere —
     then runs `b2_attention_rows_fwd` over its two query chunks in one launch
-    (the later, heavier chunk's tiles first). Two flag
-    barriers per layer (b2_peer_barrier): peers are done reading their QKV buffers before they are
-    written, and every chunk has landed before attention reads it. The output is gathered to every
+    (the later, heavier chunk's tiles first). Alternate layers use two QKV copies, so one flag
+    barrier per layer (b2_peer_barrier, after the QKV GEMM: every chunk has landed before attention
+    reads it) also orders the writes of layer i against the reads of layer i - 2 (at 8 GPUs the
+    per-layer barriers cost 0.87 ms per C4 step with two per layer). The output is gathered to every
     rank the same way. Built from the full model's state dict (reference key names).
     """
 
@@ -420,12 +421,16 @@ class ContextParallelTransformer:
         self._buf = None
         d = self.config.d_model
         tokens = batch * seq_len
+        # Two full-length QKV copies, used by alternate layers: a rank writes layer i's K/V into
+        # copy i % 2 of every peer, which the peers last read for layer i - 2's attention — over
+        # before they arrived at layer i - 1's barrier (each barrier kernel waits for its stream's
+        # earlier kernels), so one barrier per layer orders every reader against every writer.
         n_qkv, n_out = tokens * 3 * d, tokens * d
-        buf = symm_mem.empty(n_qkv + n_out + 64, dtype=torch.bfloat16, device=self.device)
-        buf[n_qkv + n_out:].zero_()
+        buf = symm_mem.empty(2 * n_qkv + n_out + 64, dtype=torch.bfloat16, device=self.device)
+        buf[2 * n_qkv + n_out:].zero_()
         group = self.group if self.group is not None else dist.group.WORLD
         handle = symm_mem.rendezvous(buf, group)
-        total = n_qkv + n_out + 64
+        total = 2 * n_qkv + n_out + 64
         peers = [handle.get_buffer(r, (total,), torch.bfloat16) for r in range(self.world)]
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)  # every pad is zero before any rank signals
@@ -434,9 +439,10 @@ class ContextParallelTransformer:
         self._buf = {
             "shape": (batch, seq_len), "buf": buf, "handle": handle, "chunk": chunk, "mine": mine,
             "pieces": pieces,
-            "qkv": [p[:n_qkv].view(tokens, 3 * d) for p in peers],  # every rank's QKV buffer
-            "out": [p[n_qkv:n_qkv + n_out].view(tokens, d) for p in peers],
-            "pads": [int(x) + (n_qkv + n_out) * 2 for x in handle.buffer_ptrs],
+            # [copy][rank]: every rank's two QKV buffers
+            "qkv": [[p[c * n_qkv:(c + 1) * n_qkv].view(tokens, 3 * d) for p in peers] for c in range(2)],
+            "out": [p[2 * n_qkv:2 * n_qkv + n_out].view(tokens, d) for p in peers],
+            "pads": [int(x) + (2 * n_qkv + n_out) * 2 for x in handle.buffer_ptrs],
             "ctx": torch.empty(tokens, d, device=self.device, dtype=torch.bfloat16),
         }
         return self._buf
@@ -460,8 +466,7 @@ class ContextParallelTransformer:
         kv_len, row_mask = self._mask_lengths(valid_token_mask, batch, seq_len)
         sb = self._buffers(batch, seq_len)
         pieces, chunk, pads = sb["pieces"], sb["chunk"], sb["pads"]
-        qkv_all, out_all, ctx = sb["qkv"], sb["out"], sb["ctx"]
-        qkv = qkv_all[self.rank]
+        qkv_copies, out_all, ctx = sb["qkv"], sb["out"], sb["ctx"]
         h, hd = cfg.num_heads, cfg.head_dim
         t_loc = len(pieces) * chunk
         dev = x.device
@@ -499,7 +504,8 @@ class ContextParallelTransformer:
         for i, pb in enumerate(packed):
             if i > 0:
                 t("layernorm", _capi.layernorm, resid, pb.ln1_w, pb.ln1_b, pb.ln1_eps, ln)
-            barrier()  # peers are done reading their QKV buffers (previous layer's attention)
+            qkv_all = qkv_copies[i % 2]  # copy i % 2: its readers (layer i - 2) are done, see _buffers
+            qkv = qkv_all[self.rank]
             for k in range(len(pieces)):  # K and V columns also stored into every peer's buffer
                 row0 = pieces[k][0]
                 t("gemm_qkv", _capi.linear_bcast, local(ln, k), pb.w_qkv, pb.b_qkv,
@@ -529,10 +535,10 @@ class ContextParallelTransformer:
 
     def launches_per_forward(self, num_layers: int) -> int:
         """Kernels of this library per forward (copies not counted): per layer one QKV and one
-        out_proj GEMM per piece (2 pieces per sequence), 1 attention launch, 2 barriers,
+        out_proj GEMM per piece (2 pieces per sequence), 1 attention launch, 1 barrier,
         LayerNorm x 2, ffn_in, ffn_out; then the final LayerNorm and 2 barriers."""
         p = 2 * self.config.batch_size
-        return num_layers * (2 * p + 7) + 3
+        return num_layers * (2 * p + 6) + 3
 
     def close(self) -> None:
         """Drops the symmetric-memory buffers (call on every rank before destroying the group)."""
