@@ -36,7 +36,7 @@ import torch.nn as nn
 from . import _capi
 from .cases import TransformerConfig, config_from
 
-# 64 and 128 run on the tcgen05 attention kernel; 8, 16, 32 and 256 (the reference's official
+# 32, 64 and 128 run on the tcgen05 attention kernels; 8, 16 and 256 (the reference's official
 # case matrix) on the CUDA-core one.
 SUPPORTED_HEAD_DIMS = (8, 16, 32, 64, 128, 256)
 
