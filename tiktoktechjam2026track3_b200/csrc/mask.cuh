@@ -17,8 +17,9 @@ constexpr int kMaskThreads = 256;
 __global__ void __launch_bounds__(kMaskThreads)
     mask_lengths_kernel(const uint8_t* __restrict__ mask, int64_t seq_len, int32_t* __restrict__ kv_len,
                         uint8_t* __restrict__ row_copy, uint8_t* __restrict__ not_prefix) {
+  // No early launch of the dependent kernel: the attention kernels read kv_len in their prologue,
+  // before their own wait for this grid, so the next launch starts only once this one has ended.
   pdl_wait_previous_grid();
-  pdl_allow_next_grid();
   __shared__ int warp_sums[kMaskThreads / 32];
   __shared__ int warp_bad[kMaskThreads / 32];
   const int64_t b = blockIdx.x;
