@@ -99,7 +99,7 @@ def test_gemm_bias_gelu(m, n, k):
 def test_gelu_epilogue_against_exact_gelu():
     """GELU on exactly representable GEMM outputs (A @ I) against float64 exact-erf GELU.
 
-    The epilogue evaluates erf with a rational-exponential formula (|error| <= 1.5e-7) in fp32,
+    The epilogue evaluates erf with a rational formula (|error| <= 3e-7) in fp32,
     so 0.5 x (1 + erf) keeps fp32's absolute cancellation error (~1e-7 |x|) in the negative tail,
     as ATen's fp32 GELU does; elsewhere the result is the correctly rounded bf16 value or one ulp
     away when the exact value sits next to a rounding boundary."""
