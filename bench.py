@@ -53,6 +53,7 @@ if str(ROOT) not in sys.path:
 
 from tiktoktechjam2026track3_b200 import UserOptimizedTransformer  # noqa: E402
 from tiktoktechjam2026track3_b200.cases import BASELINE_CONFIGS, TransformerConfig, generate_random_case  # noqa: E402
+from tiktoktechjam2026track3_b200.models import attention_kernel_name  # noqa: E402
 
 METRIC = "forward_tokens_per_sec"
 UNIT = "tokens/s"
@@ -534,8 +535,8 @@ def main() -> None:
         "gemm_tc_kernel": {"ms": sum(v for k, v in kind_ms.items() if k.startswith("gemm")), "work": gemm_total,
                            "bound": "tensor",
                            "launches": sum(v for k, v in kind_n.items() if k.startswith("gemm"))},
-        "attention_pair_kernel": {"ms": kind_ms.get("attention", 0.0), "work": attn, "bound": "tensor",
-                                  "launches": kind_n.get("attention", 0)},
+        attention_kernel_name(cfg.head_dim): {"ms": kind_ms.get("attention", 0.0), "work": attn, "bound": "tensor",
+                                               "launches": kind_n.get("attention", 0)},
         "layernorm_vec_kernel": {"ms": kind_ms.get("layernorm", 0.0), "work": layernorm_bytes(cfg, ln_fused),
                                  "bound": "hbm", "launches": kind_n.get("layernorm", 0)},
     }

@@ -41,6 +41,15 @@ from .cases import TransformerConfig, config_from
 SUPPORTED_HEAD_DIMS = (8, 16, 32, 64, 128, 256)
 
 
+def attention_kernel_name(head_dim: int) -> str:
+    """The attention kernel b2_attention_fwd launches for `head_dim` (its dispatch in b200tx.cu)."""
+    if head_dim in (32, 64):
+        return "attention_solo_kernel"
+    if head_dim == 128:
+        return "attention_pair_kernel"
+    return "attention_simt_kernel"
+
+
 class SelfAttention(nn.Module):
     """Parameter holder with BaselineSelfAttention's names (models.py:20-33)."""
 
