@@ -45,9 +45,31 @@ import time
 from datetime import timedelta
 from pathlib import Path
 
-import torch
+# NCCL writes its version banner and log lines to stdout (the banner even at NCCL_DEBUG=WARN) and
+# fixes its log file when the library first initialises, which can happen while torch imports:
+# send them to stderr before torch is imported, so that stdout carries only the one JSON line.
+os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+
+import torch  # noqa: E402
 
 ROOT = Path(__file__).resolve().parent
+
+
+class stdout_to_stderr:
+    """Points file descriptor 1 at stderr for the duration (output of native libraries included)."""
+
+    def __enter__(self):
+        sys.stdout.flush()
+        self._saved = os.dup(1)
+        os.dup2(2, 1)
+        return self
+
+    def __exit__(self, *exc):
+        sys.stdout.flush()
+        os.dup2(self._saved, 1)
+        os.close(self._saved)
+        return False
+
 if str(ROOT) not in sys.path:
     sys.path.insert(0, str(ROOT))
 
@@ -385,10 +407,11 @@ def main() -> None:
     if world > 1:
         import torch.distributed as dist
 
-        # NCCL writes its banner and log lines to stdout (even the version line at WARN): send them
-        # to stderr, so that stdout carries only the one JSON line.
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+        # The communicator is created here (device_id: eager init) and by the first barrier; anything
+        # NCCL prints to file descriptor 1 while it starts goes to stderr.
+        with stdout_to_stderr():
+            dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+            dist.barrier()
 
     weak = args.per_gpu_batch > 0
     gcfg, pad = workload_config(args.workload, args.per_gpu_batch * world if weak else 0)
