@@ -208,6 +208,12 @@ ATTN_CASES = [
     # fit one wave either way and run one tile per CTA): even and odd tile counts
     (8, 1024, 16, 64, True, None),
     (4, 1152, 16, 128, False, [1152, 1000, 640, 129]),
+    # C2's shape with its padding lengths, causal with padding and ragged lengths (head_dim 64 and
+    # 32), a sequence shorter than one query tile
+    (8, 512, 12, 64, False, [256, 511, 384, 300, 512, 257, 449, 320]),
+    (3, 500, 5, 64, True, [500, 257, 64]),
+    (4, 448, 6, 32, True, [448, 65, 1, 200]),
+    (1, 65, 1, 64, True, None),
     # CUDA-core kernel (head dims of the reference's official case matrix)
     (2, 128, 4, 32, True, None),
     (3, 200, 4, 8, False, [200, 77, 1]),
