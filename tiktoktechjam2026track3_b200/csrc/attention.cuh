@@ -1,7 +1,7 @@
 // Flash-style multi-head self-attention forward: the shared parameters, the host entry point,
-// and the softmax wait helper. The tcgen05 kernels are in attention_solo.cuh (head_dim 32 and 64,
-// one query tile per CTA, two CTAs per SM) and attention_pair.cuh (head_dim 128, two query tiles
-// per CTA); head dims 8, 16 and 256 run on CUDA cores (attention_simt.cuh).
+// and the softmax helpers. The tcgen05 kernels are in attention_solo.cuh (head_dim 32 and 64,
+// one query tile per CTA, two CTAs per SM) and attention_wide.cuh (head_dim 128, one query tile
+// per CTA with three score buffers); head dims 8, 16 and 256 run on CUDA cores (attention_simt.cuh).
 //
 // Computes, per batch b, head h and query q (BaselineSelfAttention.forward,
 // transformer_benchmark/models.py:55-75):
@@ -39,9 +39,6 @@ struct AttnParams {
   int q_tile0[2];    // first query tile (128 rows) of the range
   int n_q_tiles[2];  // query tiles in the range
   int q_end[2];      // one past the last query row of the range
-  // Query tiles per CTA of the tensor-core kernel: 2 (one per softmax group) or 1 (group 1 idle),
-  // chosen at launch by the wave count (attention_pair_tiles_per_cta).
-  int tiles_per_cta;
   // Grid order of the tensor-core kernels: 1 = query blocks along x and (b, h) along y, so the
   // hardware issues every query block of one head (heaviest first) before the next head and the
   // CTAs resident at any time read the K/V rows of one or two heads, which stay in L2 (a
@@ -80,6 +77,19 @@ __device__ __forceinline__ int attn_range_of(const AttnParams& p, int y, const i
   return 0;
 }
 
+// Row maximum of 32 values as a balanced tree of 3-input maxima (short dependency chains).
+__device__ __forceinline__ float max32(const float* v) {
+  float a[11];
+#pragma unroll
+  for (int i = 0; i < 10; ++i) a[i] = max3f(v[3 * i], v[3 * i + 1], v[3 * i + 2]);
+  a[10] = fmaxf(v[30], v[31]);
+  const float b0 = max3f(a[0], a[1], a[2]);
+  const float b1 = max3f(a[3], a[4], a[5]);
+  const float b2 = max3f(a[6], a[7], a[8]);
+  const float b3 = fmaxf(a[9], a[10]);
+  return fmaxf(max3f(b0, b1, b2), b3);
+}
+
 // Softmax-warp wait: once any wait of this thread gave up (`alive` false) later waits are
 // skipped, so the warp still runs its remaining iterations and every named barrier stays matched.
 __device__ __forceinline__ void softmax_wait(uint64_t* bar, uint32_t parity, uint32_t site, bool& alive,
@@ -94,14 +104,13 @@ cudaError_t make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner
                               uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer);
 
 template <int HD>
-static cudaError_t launch_attention_pair(const CUtensorMap& tm, const AttnParams& p, cudaStream_t stream);
-
-template <int HD>
 static cudaError_t launch_attention_simt(const __nv_bfloat16* qkv, int64_t ld_qkv, const AttnParams& p,
                                          cudaStream_t stream);
 
 template <int HD>
 static cudaError_t launch_attention_solo(const CUtensorMap& tm, const AttnParams& p, cudaStream_t stream);
+
+static cudaError_t launch_attention_wide(const CUtensorMap& tm, const AttnParams& p, cudaStream_t stream);
 
 
 cudaError_t launch_attention(const __nv_bfloat16* qkv, int64_t ld_qkv, int64_t q_col, int64_t k_col, int64_t v_col,
@@ -126,7 +135,6 @@ cudaError_t launch_attention(const __nv_bfloat16* qkv, int64_t ld_qkv, int64_t q
   p.causal = causal;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.n_ranges = n_ranges;
-  p.tiles_per_cta = 2;
   p.head_major = (S >= 16384 && B * H <= 65535) ? 1 : 0;
   for (int r = 0; r < 2; ++r) {
     const int64_t q_begin = r < n_ranges ? q_ranges[2 * r] : 0;
@@ -152,7 +160,7 @@ cudaError_t launch_attention(const __nv_bfloat16* qkv, int64_t ld_qkv, int64_t q
   if (e != cudaSuccess) return e;
   if (hd == 32) return launch_attention_solo<32>(tm, p, stream);
   if (hd == 64) return launch_attention_solo<64>(tm, p, stream);
-  return launch_attention_pair<128>(tm, p, stream);
+  return launch_attention_wide(tm, p, stream);
 }
 
 }  // namespace b2

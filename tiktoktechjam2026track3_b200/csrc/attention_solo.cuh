@@ -2,37 +2,37 @@
 // BaselineSelfAttention.forward, transformer_benchmark/models.py:55-75; masks as in attention.cuh).
 //
 // For short sequences the work of a layer is a few hundred query tiles of 2-4 KV tiles each
-// (C2: 8 x 512 tokens, 12 heads, padded lengths in [256, 512]). The two-tile kernel
-// (attention_pair.cuh) then runs as two waves of long-latency CTAs: its 384 threads x 168
-// registers and 160 KB of shared memory keep one CTA per SM, and a per-CTA trace showed each CTA
-// spending ~2.4 us waiting for its first Q tile and ~1.7 us per KV tile on its chain of
-// S = Q K^T -> row max -> exponentials -> O += P V, with the second wave starting only when the
-// first has drained. This kernel is the same computation for one query tile with 6 warps
-// (192 threads x 168 registers), 80 KB of shared memory (2-stage K and V rings) and 256 TMEM
-// columns, so that two CTAs share an SM: their chains interleave on the tensor core and the
-// exponential unit without any ping-pong between them, and a CTA of the next wave starts as soon
-// as either resident CTA ends.
+// (C2: 8 x 512 tokens, 12 heads, padded lengths in [256, 512]). A kernel with two query tiles per
+// CTA (384 threads x 168 registers, 160 KB of shared memory, one CTA per SM, its two softmax
+// groups alternating on the exponential unit) ran them as two waves of long-latency CTAs: a
+// per-CTA trace showed each CTA spending ~2.4 us waiting for its first Q tile and ~1.7 us per KV
+// tile on its chain of S = Q K^T -> row max -> exponentials -> O += P V, with the second wave
+// starting only when the first had drained. This kernel is the same computation for one query
+// tile with 6 warps (192 threads x 168 registers), 80 KB of shared memory (2-stage K and V rings)
+// and 256 TMEM columns, so that two CTAs share an SM: their chains interleave on the tensor core
+// and the exponential unit without any ping-pong between them, and a CTA of the next wave starts
+// as soon as either resident CTA ends.
 //
 //   warp 0      TMA: Q once; K_j and V_j (128 keys) into two independent 2-stage rings.
 //   warp 1      TMEM allocator and UMMA issuer: S(j) = Q K_j^T into TMEM once S(j-1) has been
 //               read (s_free), then O += P(j-1) V_{j-1} once P(j-1) is published (p_full), P read
 //               from TMEM as the A operand.
 //   warps 2..5  softmax, one query row per thread (warp % 4 = TMEM lane quadrant): row maximum
-//               from the scores in TMEM, exp2(c s - c m) written as bf16 pairs into P in TMEM
-//               after O += P(j-1) V has landed (o_full), fp32 row sums in registers, the same lazy
-//               rescale as the two-tile kernel (reference maximum moves only by more than 2^8).
+//               from the scores in TMEM, exp2(c s - c m) computed into registers as bf16 pairs
+//               and stored into P in TMEM after O += P(j-1) V has landed (o_full), fp32 row sums
+//               in registers, lazy rescale (the reference maximum moves only by more than 2^8).
 // Tensor memory: S (128 columns) at 0, P (128 bf16 keys in 64 columns) at 128, O (64) at 192.
 // Measured on one B200 against the two-tile kernel (CUDA events, L2 flushed): C2's attention
 // (B=8, S=512, 12 heads, padded) 33.3 -> 28.3 us, B=16 S=2048 causal 321 -> 254 us, B=1 S=16384
 // causal 871 -> 743 us (631 -> 740 TFLOP/s): two softmax warps per SM sub-partition keep the
 // exponential unit busier than the two-tile kernel's ping-pong between its groups. At C5 (4 x 100000
 // tokens, ~110 ms per launch at the 1000 W power cap) with the head-major grid order it runs at
-// 752 TFLOP/s against 672 for the two-tile kernel (692 without its register split): with K/V
-// served from L2, streaming them once per query tile no longer costs more than the scheduling
-// gains. It is the head_dim-64 kernel for every shape. Computing the exponentials of tile j into
-// registers before waiting for O += P(j-1) V (only the store into P waits) gave, with bit-identical
-// outputs: B=16 S=2048 causal 247.8 -> 239.6 us, B=1 S=16384 841.7 -> 825.3 us, 4 x 100000 causal
-// 106.8 -> 105.6 ms, head_dim 32 (B=64 S=1024, 4 heads) 82.0 -> 79.9 us; C2's shape unchanged.
+// 752 TFLOP/s against 672 for the two-tile kernel: with K/V served from L2, streaming them once
+// per query tile no longer costs more than the scheduling gains. It is the head_dim-64 kernel for
+// every shape. Computing the exponentials of tile j into registers before waiting for
+// O += P(j-1) V (only the store into P waits) gave, with bit-identical outputs: B=16 S=2048 causal
+// 247.8 -> 239.6 us, B=1 S=16384 841.7 -> 825.3 us, 4 x 100000 causal 106.8 -> 105.6 ms, head_dim
+// 32 (B=64 S=1024, 4 heads) 82.0 -> 79.9 us; C2's shape unchanged.
 #pragma once
 #include "b2_common.cuh"
 #include "attention.cuh"
@@ -379,10 +379,8 @@ static cudaError_t launch_attention_solo(const CUtensorMap& tm, const AttnParams
                                     Cfg::kSmemBytes);
   });
   if (attr_err != cudaSuccess) return attr_err;
-  AttnParams q = p;
-  q.tiles_per_cta = 1;
-  const dim3 grid = attn_grid(q, static_cast<unsigned>(p.n_q_tiles[0] + (p.n_ranges > 1 ? p.n_q_tiles[1] : 0)));
-  return launch_pdl(attention_solo_kernel<HD>, grid, dim3(Cfg::kThreads), Cfg::kSmemBytes, stream, tm, q);
+  const dim3 grid = attn_grid(p, static_cast<unsigned>(p.n_q_tiles[0] + (p.n_ranges > 1 ? p.n_q_tiles[1] : 0)));
+  return launch_pdl(attention_solo_kernel<HD>, grid, dim3(Cfg::kThreads), Cfg::kSmemBytes, stream, tm, p);
 }
 
 }  // namespace b2

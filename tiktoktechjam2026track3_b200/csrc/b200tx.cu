@@ -20,8 +20,8 @@
 #include "layernorm.cuh"
 #include "gemm.cuh"
 #include "attention.cuh"
-#include "attention_pair.cuh"
 #include "attention_solo.cuh"
+#include "attention_wide.cuh"
 #include "attention_simt.cuh"
 #include "peer.cuh"
 #include "mask.cuh"

@@ -46,7 +46,7 @@ def attention_kernel_name(head_dim: int) -> str:
     if head_dim in (32, 64):
         return "attention_solo_kernel"
     if head_dim == 128:
-        return "attention_pair_kernel"
+        return "attention_wide_kernel"
     return "attention_simt_kernel"
 
 
