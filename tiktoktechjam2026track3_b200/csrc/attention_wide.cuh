@@ -15,13 +15,17 @@
 // non-causal B=2 S=2048 unchanged (101 us). One pair in four of the exponentials on the FMA pipe
 // (exp2_poly_x2) then gave 4106 -> 4077 us at C4's shape and 300 -> 293 us at S=8192 (one in two
 // was slower); splitting each row's 128 keys between two softmax warps (320 threads, a row-maximum
-// exchange per tile) was measured slower (4115 us).
+// exchange per tile) was measured slower (4115 us). Issuing S = Q K^T and O += P V from two
+// threads instead of one (a thread's back-to-back tcgen05.mma take at least ~114 clocks each at
+// N <= 128, so one issuer left the tensor core idle between instructions) then gave 4005 -> 3861 us
+// at C4's shape and 299 -> 282 us at S=8192, bit-identical.
 //
 //   warp 0      TMA: Q once (two 64-column boxes); K_j and V_j (128 keys x 128 dims, two boxes
 //               each) into two 3-stage rings.
-//   warp 1      TMEM allocator and UMMA issuer: S(0), S(1), then per tile O += P(j) V_j once P(j) is
-//               published, followed by S(j+2) into the buffer P(j-1) occupied (P(j) published means
-//               O += P(j-1) V completed: the softmax waits for it before storing P(j)).
+//   warp 1      TMEM allocator and issuer of S: S(0), S(1), then S(j+2) into the buffer P(j-1)
+//               occupied once P(j) is published (which means O += P(j-1) V completed: the softmax
+//               waits for it before storing P(j)).
+//   warp 6      issuer of O += P(j) V_j once P(j) is published.
 //   warps 2..5  softmax, one query row per thread (warp % 4 = TMEM lane quadrant): row maximum,
 //               exp2(c s - c m) into registers as bf16 pairs, then (after O += P(j-1) V has landed)
 //               the pairs into P and, when the reference maximum moved by more than 2^8, O rescaled.
@@ -34,7 +38,8 @@
 namespace b2 {
 
 struct AttnWideCfg {
-  static constexpr int kThreads = 192;
+  static constexpr int kThreads = 224;
+  static constexpr int kPvWarp = 6;  // O += P V issuer (warps 2..5 are the softmax)
   static constexpr int kBoxBytes = 128 * 128;     // 128 rows x 64 bf16 columns (one TMA box)
   static constexpr int kTileBytes = 2 * kBoxBytes;  // 128 rows x 128 bf16 columns
   static constexpr int kStages = 3;
@@ -104,7 +109,7 @@ __global__ void __launch_bounds__(AttnWideCfg::kThreads, 1)
       mbar_init(&p_full[i], 4);
     }
     mbar_init(o_full, 1);
-    mbar_init(drain, 1);
+    mbar_init(drain, 2);  // one commit from each issuer
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -180,57 +185,67 @@ __global__ void __launch_bounds__(AttnWideCfg::kThreads, 1)
           drain_wait(&v_full[j % Cfg::kStages], (j / Cfg::kStages) & 1);
       }
     }
-  } else if (warp == 1) {
-    // ---------------- UMMA issuer ----------------
+  } else if (warp == 1 || warp == Cfg::kPvWarp) {
+    // ---------------- UMMA issuers ----------------
+    // Two threads issue: warp 1 the products S = Q K^T, warp kPvWarp the products O += P V. One
+    // thread's back-to-back tcgen05.mma take at least ~114 clocks each at N <= 128 (measured on
+    // B200), so with one issuer the tensor core idles between the instructions of each product;
+    // two issuers keep both products in flight. Each commit tracks its own thread's MMAs only.
     if (lane == 0) {
-      constexpr uint32_t idesc_s = make_idesc_bf16_f32(128, 128, 0, 0);
-      constexpr uint32_t idesc_o = make_idesc_bf16_f32(128, HD, 0, 1);
-      const uint32_t q_addr = smem_u32(s_q);
-      const uint32_t d_o = tmem_base + Cfg::kOCol;
-      // S(j) into buffer j mod 3 (K_j loaded; the buffer's previous P, P(j-3), was consumed by an
-      // O += P V that completed before P(j-1) was published, which the caller has waited for).
-      auto issue_s = [&](int j) -> bool {
-        const int st = j % Cfg::kStages;
-        if (!mbar_wait(&k_full[st], (j / Cfg::kStages) & 1, abort_flag, kKernelAttention, 72)) return false;
-        tc_fence_after_sync();
-        const uint32_t k_addr = smem_u32(s_k + st * Cfg::kTileBytes);
-        const uint32_t d_s = tmem_base + (j % Cfg::kBufs) * 128;
+      bool ok = true;
+      if (warp == 1) {
+        constexpr uint32_t idesc_s = make_idesc_bf16_f32(128, 128, 0, 0);
+        const uint32_t q_addr = smem_u32(s_q);
+        // S(j) into buffer j mod 3 once K_j is loaded.
+        auto issue_s = [&](int j) -> bool {
+          const int st = j % Cfg::kStages;
+          if (!mbar_wait(&k_full[st], (j / Cfg::kStages) & 1, abort_flag, kKernelAttention, 72)) return false;
+          tc_fence_after_sync();
+          const uint32_t k_addr = smem_u32(s_k + st * Cfg::kTileBytes);
+          const uint32_t d_s = tmem_base + (j % Cfg::kBufs) * 128;
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * Cfg::kBoxBytes + (kk & 3) * 32;
-          umma_bf16_ss(d_s, make_sdesc_sw128(q_addr + off, 16, 1024), make_sdesc_sw128(k_addr + off, 16, 1024),
-                       idesc_s, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * Cfg::kBoxBytes + (kk & 3) * 32;
+            umma_bf16_ss(d_s, make_sdesc_sw128(q_addr + off, 16, 1024), make_sdesc_sw128(k_addr + off, 16, 1024),
+                         idesc_s, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[j % Cfg::kBufs]);
+          umma_commit(&k_empty[st]);
+          return true;
+        };
+        ok = mbar_wait(q_full, 0, abort_flag, kKernelAttention, 75);
+        for (int j = 0; j < 2 && j < n && ok; ++j) ok = issue_s(j);
+        for (int j = 0; j + 2 < n && ok; ++j) {
+          // Buffer (j + 2) mod 3 held P(j-1): P(j) published means O += P(j-1) V completed (the
+          // softmax waits for it before storing P(j)).
+          ok = mbar_wait(&p_full[j % Cfg::kBufs], (j / Cfg::kBufs) & 1, abort_flag, kKernelAttention, 79) &&
+               issue_s(j + 2);
         }
-        umma_commit(&s_full[j % Cfg::kBufs]);
-        umma_commit(&k_empty[st]);
-        return true;
-      };
-      // O += P(j) V_j: A = P from tensor memory (16 keys = 8 packed columns per step), B = V_j
-      // (MN-major: 64-wide swizzle atoms of head dims one box apart; 16 keys = 2048 bytes per step).
-      auto issue_o = [&](int j) -> bool {
-        const int st = j % Cfg::kStages;
-        const int buf = j % Cfg::kBufs;
-        if (!mbar_wait(&p_full[buf], (j / Cfg::kBufs) & 1, abort_flag, kKernelAttention, 73) ||
-            !mbar_wait(&v_full[st], (j / Cfg::kStages) & 1, abort_flag, kKernelAttention, 74))
-          return false;
-        tc_fence_after_sync();
-        const uint32_t v_addr = smem_u32(s_v + st * Cfg::kTileBytes);
-        const uint32_t a_p = tmem_base + buf * 128;
+      } else {
+        constexpr uint32_t idesc_o = make_idesc_bf16_f32(128, HD, 0, 1);
+        const uint32_t d_o = tmem_base + Cfg::kOCol;
+        // O += P(j) V_j: A = P from tensor memory (16 keys = 8 packed columns per step), B = V_j
+        // (MN-major: 64-wide swizzle atoms of head dims one box apart; 16 keys = 2048 bytes per step).
+        for (int j = 0; j < n && ok; ++j) {
+          const int st = j % Cfg::kStages;
+          const int buf = j % Cfg::kBufs;
+          if (!mbar_wait(&p_full[buf], (j / Cfg::kBufs) & 1, abort_flag, kKernelAttention, 73) ||
+              !mbar_wait(&v_full[st], (j / Cfg::kStages) & 1, abort_flag, kKernelAttention, 74)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after_sync();
+          const uint32_t v_addr = smem_u32(s_v + st * Cfg::kTileBytes);
+          const uint32_t a_p = tmem_base + buf * 128;
 #pragma unroll
-        for (int kk = 0; kk < 128 / 16; ++kk)
-          umma_bf16_ts(d_o, a_p + kk * 8, make_sdesc_sw128(v_addr + kk * 2048, Cfg::kBoxBytes, 1024), idesc_o,
-                       (j > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(o_full);
-        umma_commit(&v_empty[st]);
-        return true;
-      };
-      bool ok = mbar_wait(q_full, 0, abort_flag, kKernelAttention, 75);
-      for (int j = 0; j < 2 && j < n && ok; ++j) ok = issue_s(j);
-      for (int j = 0; j < n && ok; ++j) {
-        ok = issue_o(j);
-        // Buffer (j + 2) mod 3 held P(j-1), whose O += P(j-1) V completed before P(j) was published.
-        if (ok && j + 2 < n) ok = issue_s(j + 2);
+          for (int kk = 0; kk < 128 / 16; ++kk)
+            umma_bf16_ts(d_o, a_p + kk * 8, make_sdesc_sw128(v_addr + kk * 2048, Cfg::kBoxBytes, 1024), idesc_o,
+                         (j > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(o_full);
+          umma_commit(&v_empty[st]);
+        }
       }
+      // Both issuers commit; the barrier completes once every MMA of the CTA has.
       umma_commit(drain);
       const uint64_t t0 = global_timer_ns();
       const uint64_t lim = wait_limit_ns();
