@@ -34,3 +34,27 @@ def test_double_buffered_gemm_epilogues_do_not_spill(tmp_path):
             stores, loads = map(int, re.findall(r"(\d+) bytes spill (?:stores|loads)", line))
             assert stores == 0 and loads == 0, (current, line)
     assert checked >= 12
+
+
+def test_attention_kernels_do_not_spill(tmp_path):
+    """The tensor-core attention kernels hold a row's scores (and their packed exponentials) in
+    registers across a tile; a spill there costs local-memory traffic on every score tile."""
+    cmd = [nvcc_path(), *ARCH_FLAGS, "-O3", "-std=c++17", "-Xptxas=-v", "-Xcompiler", "-fPIC", "-shared",
+           "-o", str(tmp_path / "probe.so"), str(CSRC_DIR / "b200tx.cu")]
+    proc = subprocess.run(cmd, capture_output=True, text=True)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    current = None
+    seen = set()
+    for line in proc.stderr.splitlines():
+        m = re.search(r"Compiling entry function '(\S+)'", line)
+        if m:
+            current = m.group(1)
+            continue
+        if current is None or "spill" not in line:
+            continue
+        k = re.search(r"attention_(solo|wide)_kernel", current)
+        if k:
+            seen.add(k.group(1))
+            stores, loads = map(int, re.findall(r"(\d+) bytes spill (?:stores|loads)", line))
+            assert stores == 0 and loads == 0, (current, line)
+    assert seen == {"solo", "wide"}
